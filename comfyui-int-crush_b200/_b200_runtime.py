@@ -1,0 +1,418 @@
+"""B200 kernel runtime: the drop-in replacement of ``_triton_runtime``.
+
+Exports the same module attributes as the reference's
+``_triton_runtime.py:16-41,114-130`` -- the availability flags
+``TRITON_AVAILABLE, TRITON_INT4_UNPACK, TRITON_INT8_GEMM,
+TRITON_INT4_INT8_UNPACK, TRITON_DYNQUANT, TRITON_W4A8_GEMM, TRITON_FUSED_QGD``,
+the toggles ``USE_FUSED_W8A8`` and ``USE_CUDA_GRAPHS`` (env
+``INTCRUSH_NO_CUDA_GRAPHS=1`` disables graphs, ``_triton_runtime.py:60-61``) and
+the six kernel callables with their signatures -- but every callable runs the
+hand-written sm_100a kernels of ``libintcrush_b200.so``.  A flag is True when
+the library loaded and a CUDA device is present.  There is no CPU fallback:
+an op given CPU tensors, or called while the library is missing, raises.
+
+New fused ops beyond the reference's set: ``prep_quantize`` (SmoothRot +
+Hadamard + pad + PermuQuant + smooth + per-token INT8 in one pass),
+``gemm_a8`` (W8A8 / W4A8 with per-channel or group scales, bias and the
+zero-point term fused), ``gemm_w4a16`` (weight-streaming W4A16 with the
+low-rank residual fused), ``lowrank_down`` / ``lowrank_add``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import logging
+import os
+
+import torch
+
+from . import _lib as L
+
+log = logging.getLogger(__name__)
+
+# ── availability flags (names of the reference runtime) ─────────────────────
+try:
+    L.lib()
+    B200_LIBRARY_LOADED = True
+    _load_error: str | None = None
+except OSError as exc:  # pragma: no cover - depends on the build
+    B200_LIBRARY_LOADED = False
+    _load_error = str(exc)
+
+B200_AVAILABLE = B200_LIBRARY_LOADED and torch.cuda.is_available()
+
+TRITON_AVAILABLE = B200_AVAILABLE
+TRITON_INT4_UNPACK = B200_AVAILABLE
+TRITON_INT8_GEMM = B200_AVAILABLE
+TRITON_INT4_INT8_UNPACK = B200_AVAILABLE
+TRITON_DYNQUANT = B200_AVAILABLE
+TRITON_W4A8_GEMM = B200_AVAILABLE
+TRITON_FUSED_QGD = B200_AVAILABLE
+
+USE_FUSED_W8A8: bool = False
+USE_CUDA_GRAPHS: bool = True
+if os.environ.get("INTCRUSH_NO_CUDA_GRAPHS", "0") == "1":
+    USE_CUDA_GRAPHS = False
+
+_DT = {torch.float16: L.IC_DTYPE_F16, torch.bfloat16: L.IC_DTYPE_BF16, torch.float32: L.IC_DTYPE_F32}
+
+
+def _p(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _need_cuda(what: str, *ts: torch.Tensor | None) -> None:
+    if not B200_LIBRARY_LOADED:
+        raise RuntimeError(f"{what}: libintcrush_b200.so is not loaded ({_load_error})")
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(f"{what}: intcrush_b200 ops run on CUDA tensors only (got {t.device})")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"{what}: tensors on different devices ({dev}, {t.device})")
+
+
+def _f32c(t: torch.Tensor | None) -> torch.Tensor | None:
+    if t is None:
+        return None
+    return t.to(torch.float32).contiguous()
+
+
+def _round16(n: int) -> int:
+    return (n + 15) // 16 * 16
+
+
+# ── activation prep ──────────────────────────────────────────────────────────
+
+def prep_quantize(
+    x: torch.Tensor,
+    *,
+    smoothrot: torch.Tensor | None = None,
+    rot_size: int = 0,
+    w_in: int | None = None,
+    perm: torch.Tensor | None = None,
+    smooth: torch.Tensor | None = None,
+    quantize: bool = True,
+    want_prep: bool = False,
+    want_rowsum: bool = False,
+    s_a_out: torch.Tensor | None = None,
+    x_int8_out: torch.Tensor | None = None,
+    x_prep_out: torch.Tensor | None = None,
+):
+    """One-pass activation prep (``_ops.py:337-365`` + ``_ops.py:529-533``) and
+    per-token INT8 quantisation (``kernels/triton_quantize.py:151-198``).
+
+    Returns ``(x_int8, s_a, x_prep, rowsum)``; entries not requested are None.
+    ``x_int8`` is ``[M, w_in]`` (a view of a buffer whose row stride is w_in
+    rounded up to 16 bytes; the padding columns hold zeros).
+    """
+    _need_cuda("prep_quantize", x, smoothrot, perm, smooth)
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    if x2.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError(f"prep_quantize: x must be float16/bfloat16, got {x2.dtype}")
+    M, K = x2.shape
+    Kr = K if not rot_size else -(-K // rot_size) * rot_size
+    w_in = Kr if w_in is None else max(int(w_in), Kr)
+    # the kernel indexes these vectors without bounds checks: check lengths here
+    if smoothrot is not None and smoothrot.numel() != K:
+        raise ValueError(f"prep_quantize: smoothrot has {smoothrot.numel()} entries, expected K={K}")
+    if perm is not None and perm.numel() != w_in:
+        raise ValueError(f"prep_quantize: perm has {perm.numel()} entries, expected w_in={w_in}")
+    if smooth is not None and smooth.numel() != w_in:
+        raise ValueError(f"prep_quantize: smooth has {smooth.numel()} entries, expected w_in={w_in}")
+    if perm is not None and perm.dtype != torch.int32:
+        perm = perm.to(torch.int32)
+    perm = None if perm is None else perm.contiguous()
+    x_int8 = s_a = x_prep = rowsum = None
+    xq_full = None
+    if quantize:
+        ldq = _round16(w_in)
+        if x_int8_out is not None:
+            xq_full = x_int8_out
+            if xq_full.shape[0] != M or xq_full.stride(0) < w_in or xq_full.dtype != torch.int8:
+                raise ValueError("prep_quantize: x_int8_out must be int8 [M, >= w_in]")
+        else:
+            xq_full = torch.empty((M, ldq), dtype=torch.int8, device=x.device)
+        s_a = s_a_out if s_a_out is not None else torch.empty(M, dtype=torch.float32, device=x.device)
+        x_int8 = xq_full[:, :w_in]
+    if want_prep:
+        x_prep = x_prep_out if x_prep_out is not None else torch.empty((M, w_in), dtype=x2.dtype, device=x.device)
+    if want_rowsum:
+        rowsum = torch.empty(M, dtype=torch.float32, device=x.device)
+    sr = _f32c(smoothrot)
+    sm = _f32c(smooth)
+    st = L.lib().ic_prep_quant(
+        _p(x2), _DT[x2.dtype], M, K, x2.stride(0), _p(sr), int(rot_size), w_in, _p(perm), _p(sm),
+        _p(xq_full), xq_full.stride(0) if xq_full is not None else 0, _p(s_a), _p(x_prep), _p(rowsum),
+        _stream(x2))
+    L.check(st, "ic_prep_quant")
+    return x_int8, s_a, x_prep, rowsum
+
+
+def dynamic_quantize_activation(
+    x: torch.Tensor,
+    s_a_out: torch.Tensor | None = None,
+    x_int8_out: torch.Tensor | None = None,
+):
+    """``kernels/triton_quantize.py:151-198``: per-token symmetric INT8.
+
+    Rounding is half-to-even with IEEE division (the reference's CPU form,
+    ``kernels/triton_quantize.py:43-54``).  Leading dimensions are restored
+    like ``_reshape_if_needed``.
+    """
+    orig = x.shape
+    x2 = x.reshape(-1, orig[-1])
+    if s_a_out is not None and s_a_out.shape != (x2.shape[0],):
+        s_a_out = None
+    if x_int8_out is not None and x_int8_out.shape != x2.shape:
+        x_int8_out = None
+    x_int8, s_a, _, _ = prep_quantize(x2, s_a_out=s_a_out, x_int8_out=x_int8_out)
+    if len(orig) > 2:
+        x_int8 = x_int8.reshape(orig)
+        s_a = s_a.reshape(orig[:-1])
+    return x_int8, s_a
+
+
+# ── GEMMs ────────────────────────────────────────────────────────────────────
+
+def gemm_a8(
+    x_int8: torch.Tensor,
+    w: torch.Tensor,
+    s_w: torch.Tensor,
+    s_a: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    out_dtype: torch.dtype = torch.bfloat16,
+    out: torch.Tensor | None = None,
+    group_size: int | None = None,
+    rowsum: torch.Tensor | None = None,
+    zp_corr: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``out = s_a[m] * sum_g s_w[n,g] * (xq @ w^T)_g + bias - rowsum (x) zp_corr``.
+
+    ``w`` is int8 ``[N, K]`` or packed INT4 uint8 ``[N, K/2]``; ``s_w`` is
+    ``[N]``/``[N,1]`` (per channel) or ``[N, G]`` (groups of ``group_size``,
+    default ``ceil(K / G)`` rounded to a multiple of 128).
+    """
+    _need_cuda("gemm_a8", x_int8, w, s_w, s_a, bias, out, rowsum, zp_corr)
+    if x_int8.dtype != torch.int8:
+        raise AssertionError(f"x_int8 must be int8, got {x_int8.dtype}")
+    M, K = x_int8.shape
+    if x_int8.stride(1) != 1:
+        x_int8 = x_int8.contiguous()
+    if w.dtype == torch.int8:
+        kind = L.IC_W_INT8
+        N = w.shape[0]
+        if w.shape[1] != K:
+            raise AssertionError(f"K mismatch: {K} vs {w.shape[1]}")
+    elif w.dtype == torch.uint8:
+        kind = L.IC_W_INT4
+        N = w.shape[0]
+        if w.shape[1] != (K + 1) // 2:
+            raise AssertionError(f"packed K mismatch: {K} vs {w.shape[1]} bytes")
+    else:
+        raise AssertionError(f"w must be int8 or uint8 (packed int4), got {w.dtype}")
+    if w.stride(1) != 1:
+        w = w.contiguous()
+    sw = s_w.to(torch.float32)
+    if sw.dim() == 1:
+        sw = sw.reshape(N, -1)
+    sw = sw.reshape(N, -1).contiguous()
+    G = sw.shape[1]
+    if G > 1 and group_size is None:
+        group_size = -(-K // G)
+    gs = int(group_size) if G > 1 else K
+    sa = s_a.to(torch.float32).contiguous()
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=x_int8.device)
+    elif out.shape != (M, N) or out.stride(1) != 1:
+        raise AssertionError(f"out shape mismatch: {tuple(out.shape)} vs ({M}, {N})")
+    b = None if bias is None else bias.contiguous()
+    rs = _f32c(rowsum)
+    zc = _f32c(zp_corr)
+    st = L.lib().ic_gemm_a8(
+        _p(x_int8), M, K, x_int8.stride(0), _p(w), kind, N, w.stride(0), _p(sw), G, gs, _p(sa),
+        _p(b), _DT[b.dtype] if b is not None else 0, _p(rs), _p(zc), _p(out), _DT[out.dtype], out.stride(0),
+        _stream(x_int8))
+    L.check(st, "ic_gemm_a8")
+    return out
+
+
+def fused_int8_gemm_dequant(
+    x_int8: torch.Tensor,
+    w_int8: torch.Tensor,
+    s_w: torch.Tensor,
+    s_a: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    out_dtype: torch.dtype = torch.bfloat16,
+    activation: int = 0,
+    residual: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``kernels/triton_int8_gemm.py:135-205`` on tcgen05 (kind::i8).
+
+    The SiLU/GELU and residual epilogues of the reference are never used by
+    its forward path (``_ops.py``) and are not built here.
+    """
+    if activation != 0 or residual is not None:
+        raise NotImplementedError("activation / residual epilogues are not part of the forward path")
+    return gemm_a8(x_int8, w_int8, s_w, s_a, bias=bias, out_dtype=out_dtype, out=out)
+
+
+def fused_w4a8_gemm_dequant(
+    x_int8: torch.Tensor,
+    w_int8: torch.Tensor,
+    s_w: torch.Tensor,
+    s_a: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    out_dtype: torch.dtype = torch.bfloat16,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``kernels/triton_w4a8_gemm.py:111-169``.  Accepts the unpacked int8
+    weights of the reference or, without materialising them, packed INT4."""
+    return gemm_a8(x_int8, w_int8, s_w, s_a, bias=bias, out_dtype=out_dtype, out=out)
+
+
+def fused_quant_int8_gemm_dequant(
+    x_fp16: torch.Tensor,
+    w_int8: torch.Tensor,
+    s_w: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    out_dtype: torch.dtype = torch.bfloat16,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``kernels/triton_int8_gemm.py:331-389``: quantise + GEMM + dequant."""
+    if x_fp16.dtype not in (torch.float16, torch.bfloat16):
+        raise AssertionError(f"x must be fp16/bf16, got {x_fp16.dtype}")
+    x_int8, s_a, _, _ = prep_quantize(x_fp16)
+    if out is not None and out.shape != (x_int8.shape[0], w_int8.shape[0]):
+        out = None
+    return gemm_a8(x_int8, w_int8, s_w, s_a, bias=bias, out_dtype=out_dtype, out=out)
+
+
+def gemm_w4a16(
+    x: torch.Tensor,
+    packed: torch.Tensor,
+    scale: torch.Tensor,
+    group_size: int | None = None,
+    bias: torch.Tensor | None = None,
+    lr_mid: torch.Tensor | None = None,
+    lr_up: torch.Tensor | None = None,
+    lr_scale: float = 1.0,
+    out: torch.Tensor | None = None,
+    K: int | None = None,
+) -> torch.Tensor:
+    """W4A16: ``fp16(x @ fp16(q * s)^T (+ bias))`` then ``+= lr_scale * lr_mid @ lr_up^T``.
+
+    Replaces ``unpack_int4_to_float16`` + ``F.linear`` (``_ops.py:473-474``)
+    and the PyTorch INT4 path (``_ops.py:483-491``).  ``x`` must be fp16.
+    """
+    _need_cuda("gemm_w4a16", x, packed, scale, bias, lr_mid, lr_up, out)
+    if x.dtype != torch.float16:
+        raise TypeError(f"gemm_w4a16: activations must be float16, got {x.dtype}")
+    x2 = x if x.stride(-1) == 1 else x.contiguous()
+    M, Kx = x2.shape
+    K = Kx if K is None else K
+    N = packed.shape[0]
+    if packed.dtype != torch.uint8 or packed.shape[1] != (K + 1) // 2:
+        raise AssertionError("packed must be uint8 [N, ceil(K/2)]")
+    sc = scale.reshape(N, -1)
+    if sc.dtype not in (torch.float16, torch.float32):
+        sc = sc.to(torch.float32)
+    sc = sc.contiguous()
+    G = sc.shape[1]
+    gs = int(group_size) if (G > 1 and group_size is not None) else (-(-K // G) if G > 1 else K)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=x.device)
+    b = None if bias is None else bias.contiguous()
+    mid = None if lr_mid is None else lr_mid.to(torch.float16).contiguous()
+    up = None if lr_up is None else lr_up.to(torch.float16).contiguous()
+    R = 0 if mid is None else mid.shape[1]
+    st = L.lib().ic_gemm_w4a16(
+        _p(x2), L.IC_DTYPE_F16, M, K, x2.stride(0), _p(packed), N, packed.stride(0), _p(sc), _DT[sc.dtype],
+        G, gs, _p(b), _DT[b.dtype] if b is not None else 0, _p(mid), _p(up), R, float(lr_scale),
+        _p(out), out.stride(0), _stream(x2))
+    L.check(st, "ic_gemm_w4a16")
+    return out
+
+
+def lowrank_down(x: torch.Tensor, down: torch.Tensor) -> torch.Tensor:
+    """``mid = fp16(x @ down^T)`` (``F.linear(x_raw, down)``, ``_ops.py:242``)."""
+    _need_cuda("lowrank_down", x, down)
+    x2 = x.reshape(-1, x.shape[-1]).to(torch.float16)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    d = down.to(torch.float16).contiguous()
+    M, K = x2.shape
+    R = d.shape[0]
+    mid = torch.empty((M, R), dtype=torch.float16, device=x.device)
+    L.check(L.lib().ic_lowrank_down(_p(x2), M, K, x2.stride(0), _p(d), R, _p(mid), _stream(x2)),
+            "ic_lowrank_down")
+    return mid
+
+
+def lowrank_add(out: torch.Tensor, mid: torch.Tensor, up: torch.Tensor, scale: float) -> torch.Tensor:
+    """In place ``out = fp16(out + scale * mid @ up^T)`` (``out.addmm_``, ``_ops.py:243``)."""
+    _need_cuda("lowrank_add", out, mid, up)
+    if out.dtype != torch.float16 or out.stride(1) != 1:
+        raise TypeError("lowrank_add: out must be a row-major float16 matrix")
+    m = mid.to(torch.float16).contiguous()
+    u = up.to(torch.float16).contiguous()
+    M, N = out.shape
+    L.check(L.lib().ic_lowrank_add(_p(out), M, N, out.stride(0), _p(m), _p(u), m.shape[1], float(scale),
+                                   _stream(out)), "ic_lowrank_add")
+    return out
+
+
+def unpack_int4_to_int8(packed: torch.Tensor, K: int) -> torch.Tensor:
+    """``kernels/triton_int4_to_int8_unpack.py:55-81``."""
+    _need_cuda("unpack_int4_to_int8", packed)
+    p = packed.contiguous()
+    N = p.shape[0]
+    out = torch.empty((N, K), dtype=torch.int8, device=p.device)
+    L.check(L.lib().ic_unpack_int4_to_int8(_p(p), N, K, p.stride(0), _p(out), _stream(p)),
+            "ic_unpack_int4_to_int8")
+    return out
+
+
+def unpack_int4_to_float16(packed: torch.Tensor, scale: torch.Tensor, K: int,
+                           group_size: int | None = None) -> torch.Tensor:
+    """``kernels/triton_int4_unpack.py:62-88`` (scale ``[N]``), extended to
+    group scales ``[N, G]``."""
+    _need_cuda("unpack_int4_to_float16", packed, scale)
+    p = packed.contiguous()
+    N = p.shape[0]
+    sc = scale.reshape(N, -1)
+    if sc.dtype not in (torch.float16, torch.float32):
+        sc = sc.to(torch.float32)
+    sc = sc.contiguous()
+    G = sc.shape[1]
+    gs = int(group_size) if group_size else -(-K // G)
+    out = torch.empty((N, K), dtype=torch.float16, device=p.device)
+    L.check(L.lib().ic_unpack_int4_to_f16(_p(p), N, K, p.stride(0), _p(sc), _DT[sc.dtype], G, gs,
+                                          _p(out), _stream(p)), "ic_unpack_int4_to_f16")
+    return out
+
+
+def device_error(clear: bool = True) -> int:
+    """Device error word of the library (1 = a bounded wait timed out)."""
+    return L.read_device_error(clear)
+
+
+__all__ = [
+    "TRITON_AVAILABLE", "TRITON_INT4_UNPACK", "TRITON_INT8_GEMM", "TRITON_INT4_INT8_UNPACK",
+    "TRITON_DYNQUANT", "TRITON_W4A8_GEMM", "TRITON_FUSED_QGD", "USE_FUSED_W8A8", "USE_CUDA_GRAPHS",
+    "B200_AVAILABLE", "B200_LIBRARY_LOADED",
+    "dynamic_quantize_activation", "fused_int8_gemm_dequant", "fused_quant_int8_gemm_dequant",
+    "fused_w4a8_gemm_dequant", "unpack_int4_to_int8", "unpack_int4_to_float16",
+    "prep_quantize", "gemm_a8", "gemm_w4a16", "lowrank_down", "lowrank_add", "device_error",
+]

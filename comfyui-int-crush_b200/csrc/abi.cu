@@ -1,0 +1,222 @@
+// extern "C" entry points of libintcrush_b200.so (declared in
+// include/intcrush_b200.h).  Each validates its arguments, launches on the
+// caller's stream and returns a status code; no exception crosses the ABI.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+#include <math.h>
+
+#include "ic_common.cuh"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return IC_OK;
+  return fail(IC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+bool is_pow2(long long v) { return v > 0 && (v & (v - 1)) == 0; }
+bool is_pow4(long long v) { return v >= 4 && is_pow2(v) && (v & 0x55555555LL) == v; }
+int ilog2(long long v) { int r = 0; while ((1LL << r) < v) ++r; return r; }
+
+// fp16(fp32(1/sqrt(n))): the Sylvester entry as the reference materialises it
+// (fp16 tensor times a Python float, _quant_utils.py:112).
+double sylvester_entry(int n) {
+  const float f = (float)(1.0 / sqrt((double)n));
+  return (double)__half2float(__float2half_rn(f));
+}
+
+}  // namespace
+
+extern "C" {
+
+int ic_version(void) { return (1 << 16) | 0; }
+
+const char* ic_last_error(void) { return g_err; }
+
+int ic_read_device_error(int clear, int* code_out) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_ic_dev_error, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "reading the device error word");
+  if (clear && v) {
+    const int z = 0;
+    e = cudaMemcpyToSymbol(g_ic_dev_error, &z, sizeof(int));
+    if (e != cudaSuccess) return cuda_status(e, "clearing the device error word");
+  }
+  if (code_out) *code_out = v;
+  return IC_OK;
+}
+
+int ic_prep_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const float* smoothrot,
+                  int rot_size, int64_t w_in, const int32_t* perm, const float* smooth, int8_t* x_int8,
+                  int64_t ldq, float* s_a, void* x_prep, float* rowsum, void* stream) {
+  g_err[0] = 0;
+  if (x_dtype != IC_DTYPE_F16 && x_dtype != IC_DTYPE_BF16)
+    return fail(IC_ERR_ARG, "ic_prep_quant: x dtype must be f16 or bf16");
+  if (M < 0 || K <= 0 || ldx < K) return fail(IC_ERR_ARG, "ic_prep_quant: bad M/K/ldx (%lld, %lld, %lld)",
+                                              (long long)M, (long long)K, (long long)ldx);
+  if (M == 0) return IC_OK;
+  if (!x) return fail(IC_ERR_ARG, "ic_prep_quant: x is NULL");
+  if (rot_size != 0 && (!is_pow2(rot_size) || rot_size < 2 || rot_size > 4096))
+    return fail(IC_ERR_ARG, "ic_prep_quant: rot_size must be 0 or a power of two in [2, 4096], got %d", rot_size);
+  const int64_t Kr = rot_size ? ((K + rot_size - 1) / rot_size) * rot_size : K;
+  if (w_in < Kr) return fail(IC_ERR_ARG, "ic_prep_quant: w_in (%lld) < rotated width (%lld)",
+                             (long long)w_in, (long long)Kr);
+  if (x_int8) {
+    if (!s_a) return fail(IC_ERR_ARG, "ic_prep_quant: s_a is required with x_int8");
+    if (ldq < w_in || (ldq % 16) != 0 || !aligned16(x_int8))
+      return fail(IC_ERR_ARG, "ic_prep_quant: ldq must be >= w_in, a multiple of 16, and x_int8 16-byte aligned");
+  }
+  if (!x_int8 && !x_prep && !rowsum) return fail(IC_ERR_ARG, "ic_prep_quant: no output requested");
+  if (w_in > 65536 || M > 0x7fffffffLL) return fail(IC_ERR_UNSUPPORTED, "ic_prep_quant: w_in > 65536 or M >= 2^31");
+  ic::PrepArgs a;
+  a.x = x; a.M = M; a.K = K; a.ldx = ldx; a.smoothrot = smoothrot; a.w_in = w_in; a.perm = perm;
+  a.smooth = smooth; a.xq = x_int8; a.ldq = ldq; a.s_a = s_a; a.x_prep = x_prep; a.rowsum = rowsum;
+  a.Kr = Kr; a.Wp = Kr > w_in ? Kr : w_in;
+  a.syl_h = (rot_size && !is_pow4(rot_size)) ? sylvester_entry(rot_size) : 0.0;
+  a.vec_ok = aligned16(x) && (ldx % 8 == 0);
+  const int log2r = rot_size ? ilog2(rot_size) : 0;
+  const bool syl = rot_size && !is_pow4(rot_size);
+  return cuda_status(ic::launch_prep(a, x_dtype, log2r, syl, (cudaStream_t)stream), "ic_prep_quant launch");
+}
+
+int ic_dynamic_quantize(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int8_t* x_int8,
+                        int64_t ldq, float* s_a, void* stream) {
+  return ic_prep_quant(x, x_dtype, M, K, ldx, nullptr, 0, K, nullptr, nullptr, x_int8, ldq, s_a, nullptr,
+                       nullptr, stream);
+}
+
+int ic_gemm_a8(const int8_t* xq, int64_t M, int64_t K, int64_t ldq, const void* w, int w_kind, int64_t N,
+               int64_t ldw, const float* s_w, int64_t G, int64_t group_size, const float* s_a,
+               const void* bias, int bias_dtype, const float* rowsum, const float* zp_corr, void* out,
+               int out_dtype, int64_t ldo, void* stream) {
+  g_err[0] = 0;
+  if (M < 0 || N < 0 || K <= 0) return fail(IC_ERR_ARG, "ic_gemm_a8: bad M/N/K");
+  if (M == 0 || N == 0) return IC_OK;
+  if (!xq || !w || !s_w || !s_a || !out) return fail(IC_ERR_ARG, "ic_gemm_a8: NULL operand");
+  if (w_kind != IC_W_INT8 && w_kind != IC_W_INT4) return fail(IC_ERR_ARG, "ic_gemm_a8: bad w_kind");
+  if (out_dtype < IC_DTYPE_F16 || out_dtype > IC_DTYPE_F32) return fail(IC_ERR_ARG, "ic_gemm_a8: bad out dtype");
+  if (bias && (bias_dtype < IC_DTYPE_F16 || bias_dtype > IC_DTYPE_F32)) return fail(IC_ERR_ARG, "ic_gemm_a8: bad bias dtype");
+  if ((rowsum == nullptr) != (zp_corr == nullptr)) return fail(IC_ERR_ARG, "ic_gemm_a8: rowsum and zp_corr go together");
+  if (ldq < K || ldq % 16 || !aligned16(xq)) return fail(IC_ERR_ARG, "ic_gemm_a8: xq needs ldq >= K, ldq %% 16 == 0, 16-byte alignment");
+  if (!aligned16(w) || ldw % 16) return fail(IC_ERR_ARG, "ic_gemm_a8: weights need 16-byte aligned base and row stride");
+  if (w_kind == IC_W_INT8 && (K % 16 || ldw < K)) return fail(IC_ERR_ARG, "ic_gemm_a8: int8 weights need K %% 16 == 0 and ldw >= K");
+  if (w_kind == IC_W_INT4 && (K % 32 || ldw < K / 2)) return fail(IC_ERR_ARG, "ic_gemm_a8: int4 weights need K %% 32 == 0 and ldw >= K/2");
+  if (ldo < N) return fail(IC_ERR_ARG, "ic_gemm_a8: ldo < N");
+  if (G < 1) return fail(IC_ERR_ARG, "ic_gemm_a8: G must be >= 1");
+  if (G > 1) {
+    if (group_size <= 0 || group_size % 128) return fail(IC_ERR_UNSUPPORTED, "ic_gemm_a8: group_size must be a multiple of 128");
+    if ((K + group_size - 1) / group_size != G) return fail(IC_ERR_ARG, "ic_gemm_a8: G != ceil(K / group_size)");
+    if (w_kind == IC_W_INT8 && group_size > 128)
+      return fail(IC_ERR_UNSUPPORTED, "ic_gemm_a8: int8 weights with group scales need group_size == 128");
+  }
+  if (M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL) return fail(IC_ERR_UNSUPPORTED, "ic_gemm_a8: dims >= 2^31");
+  ic::GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.G = (int)G; a.kb_per_group = G > 1 ? (int)(group_size / 128) : 0; a.group_size = (int)group_size;
+  a.s_w = s_w; a.s_a = s_a; a.bias = bias; a.bias_dtype = bias_dtype; a.rowsum = rowsum; a.zp_corr = zp_corr;
+  a.out = out; a.out_dtype = out_dtype; a.ldo = ldo;
+  const char* why = "kernel launch";
+  const int force_bn = 0;
+  cudaError_t e = ic::launch_gemm_a8(xq, (int)M, (int)K, ldq, w, w_kind, (int)N, ldw, a, force_bn,
+                                     (cudaStream_t)stream, &why);
+  return cuda_status(e, why);
+}
+
+int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const uint8_t* w, int64_t N,
+                  int64_t ldw, const void* scale, int scale_dtype, int64_t G, int64_t group_size,
+                  const void* bias, int bias_dtype, const void* lr_mid, const void* lr_up, int64_t R,
+                  float lr_scale, void* out, int64_t ldo, void* stream) {
+  g_err[0] = 0;
+  if (x_dtype != IC_DTYPE_F16) return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: x must be fp16");
+  if (M < 0 || N < 0 || K <= 0 || ldx < K || ldo < N) return fail(IC_ERR_ARG, "ic_gemm_w4a16: bad sizes");
+  if (M == 0 || N == 0) return IC_OK;
+  if (!x || !w || !scale || !out) return fail(IC_ERR_ARG, "ic_gemm_w4a16: NULL operand");
+  if (scale_dtype != IC_DTYPE_F16 && scale_dtype != IC_DTYPE_F32) return fail(IC_ERR_ARG, "ic_gemm_w4a16: scale dtype");
+  if (G < 1) return fail(IC_ERR_ARG, "ic_gemm_w4a16: G must be >= 1");
+  if (G > 1 && (group_size <= 0 || group_size % 128 || (K + group_size - 1) / group_size != G))
+    return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: group_size must be a multiple of 128 with G == ceil(K/group_size)");
+  if (ldw < (K + 1) / 2) return fail(IC_ERR_ARG, "ic_gemm_w4a16: ldw < ceil(K/2)");
+  if ((lr_mid == nullptr) != (lr_up == nullptr)) return fail(IC_ERR_ARG, "ic_gemm_w4a16: lr_mid and lr_up go together");
+  if (lr_mid && (R <= 0 || R > 64)) return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: low-rank R must be in [1, 64]");
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (M <= 32) {
+    ic::SkinnyArgs s;
+    s.x = (const __half*)x; s.M = (int)M; s.K = (int)K; s.ldx = ldx; s.w = w; s.N = (int)N; s.ldw = ldw;
+    s.scale = scale; s.scale_dtype = scale_dtype; s.G = (int)G; s.group_size = (int)group_size;
+    s.bias = bias; s.bias_dtype = bias_dtype; s.lr_mid = (const __half*)lr_mid; s.lr_up = (const __half*)lr_up;
+    s.R = (int)R; s.lr_scale = lr_scale; s.out = (__half*)out; s.ldo = ldo;
+    return cuda_status(ic::launch_w4a16_skinny(s, st), "ic_gemm_w4a16 (small M) launch");
+  }
+  if (K % 64 || ldx % 8 || !aligned16(x) || ldw % 16 || !aligned16(w))
+    return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: M > 32 needs K %% 64 == 0 and 16-byte aligned rows");
+  ic::GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.G = (int)G; a.group_size = (int)group_size; a.w_scale = scale; a.w_scale_dtype = scale_dtype;
+  a.bias = bias; a.bias_dtype = bias_dtype; a.out = out; a.out_dtype = IC_DTYPE_F16; a.ldo = ldo;
+  const char* why = "kernel launch";
+  cudaError_t e = ic::launch_gemm_w4a16_tc(x, (int)M, (int)K, ldx, w, (int)N, ldw, a, 0, st, &why);
+  if (e != cudaSuccess) return cuda_status(e, why);
+  if (lr_mid)
+    return cuda_status(ic::launch_lowrank_add((__half*)out, (int)M, (int)N, ldo, (const __half*)lr_mid,
+                                              (const __half*)lr_up, (int)R, lr_scale, st),
+                       "ic_gemm_w4a16 low-rank launch");
+  return IC_OK;
+}
+
+int ic_lowrank_down(const void* x, int64_t M, int64_t K, int64_t ldx, const void* down, int64_t R, void* mid,
+                    void* stream) {
+  g_err[0] = 0;
+  if (M < 0 || K <= 0 || ldx < K || R <= 0) return fail(IC_ERR_ARG, "ic_lowrank_down: bad sizes");
+  if (M == 0) return IC_OK;
+  if (!x || !down || !mid) return fail(IC_ERR_ARG, "ic_lowrank_down: NULL operand");
+  return cuda_status(ic::launch_lowrank_down((const __half*)x, (int)M, (int)K, ldx, (const __half*)down, (int)R,
+                                             (__half*)mid, (cudaStream_t)stream),
+                     "ic_lowrank_down launch");
+}
+
+int ic_lowrank_add(void* out, int64_t M, int64_t N, int64_t ldo, const void* mid, const void* up, int64_t R,
+                   float scale, void* stream) {
+  g_err[0] = 0;
+  if (M < 0 || N < 0 || ldo < N || R <= 0) return fail(IC_ERR_ARG, "ic_lowrank_add: bad sizes");
+  if (R > 64) return fail(IC_ERR_UNSUPPORTED, "ic_lowrank_add: R must be <= 64");
+  if (M == 0 || N == 0) return IC_OK;
+  if (!out || !mid || !up) return fail(IC_ERR_ARG, "ic_lowrank_add: NULL operand");
+  return cuda_status(ic::launch_lowrank_add((__half*)out, (int)M, (int)N, ldo, (const __half*)mid,
+                                            (const __half*)up, (int)R, scale, (cudaStream_t)stream),
+                     "ic_lowrank_add launch");
+}
+
+int ic_unpack_int4_to_int8(const uint8_t* packed, int64_t N, int64_t K, int64_t ldp, int8_t* out, void* stream) {
+  g_err[0] = 0;
+  if (N < 0 || K < 0 || ldp < (K + 1) / 2) return fail(IC_ERR_ARG, "ic_unpack_int4_to_int8: bad sizes");
+  if (N == 0 || K == 0) return IC_OK;
+  if (!packed || !out) return fail(IC_ERR_ARG, "ic_unpack_int4_to_int8: NULL operand");
+  return cuda_status(ic::launch_unpack_i8(packed, (int)N, (int)K, ldp, out, (cudaStream_t)stream),
+                     "ic_unpack_int4_to_int8 launch");
+}
+
+int ic_unpack_int4_to_f16(const uint8_t* packed, int64_t N, int64_t K, int64_t ldp, const void* scale,
+                          int scale_dtype, int64_t G, int64_t group_size, void* out, void* stream) {
+  g_err[0] = 0;
+  if (N < 0 || K < 0 || ldp < (K + 1) / 2 || G < 1) return fail(IC_ERR_ARG, "ic_unpack_int4_to_f16: bad sizes");
+  if (G > 1 && group_size <= 0) return fail(IC_ERR_ARG, "ic_unpack_int4_to_f16: bad group_size");
+  if (N == 0 || K == 0) return IC_OK;
+  if (!packed || !scale || !out) return fail(IC_ERR_ARG, "ic_unpack_int4_to_f16: NULL operand");
+  return cuda_status(ic::launch_unpack_f16(packed, (int)N, (int)K, ldp, scale, scale_dtype, (int)G,
+                                           (int)group_size, (__half*)out, (cudaStream_t)stream),
+                     "ic_unpack_int4_to_f16 launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,166 @@
+/*
+ * intcrush_b200 -- C ABI of the B200 (sm_100a) quantized-linear forward path.
+ *
+ * Every entry point takes raw device pointers, sizes, strides (in elements
+ * unless the name says bytes) and a cudaStream_t (passed as void*; NULL =
+ * legacy default stream).  Nothing is allocated, nothing synchronises the
+ * host: each call only enqueues kernels on `stream`, so all of them can be
+ * captured into a CUDA graph.  Each returns IC_OK or an IC_ERR_* code; the
+ * matching message is available from ic_last_error() on the calling thread.
+ *
+ * The reference interface that each entry point replaces is cited as
+ * path:line inside the ComfyUI-INT-Crush project.
+ */
+#ifndef INTCRUSH_B200_H_
+#define INTCRUSH_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* return codes */
+#define IC_OK 0
+#define IC_ERR_ARG 1          /* bad shape / stride / pointer / alignment  */
+#define IC_ERR_UNSUPPORTED 2  /* valid request outside what is built      */
+#define IC_ERR_CUDA 3         /* a CUDA runtime or driver call failed     */
+
+/* device-side error word (ic_read_device_error) */
+#define IC_DEV_ERR_NONE 0
+#define IC_DEV_ERR_TIMEOUT 1  /* a bounded mbarrier wait expired          */
+
+/* element type codes */
+#define IC_DTYPE_F16 0
+#define IC_DTYPE_BF16 1
+#define IC_DTYPE_F32 2
+
+/* weight kinds for ic_gemm_a8 */
+#define IC_W_INT8 0           /* int8  [N, K], row stride ldw bytes         */
+#define IC_W_INT4 1           /* uint8 [N, K/2] two signed nibbles per byte,
+                                 low nibble = even k (two's complement)     */
+
+/* Library version, (major << 16) | minor. */
+int ic_version(void);
+
+/* Message for the last error returned on this host thread ("" if none). */
+const char* ic_last_error(void);
+
+/* Read (and optionally clear) the device error word of the current device.
+ * Synchronises the device: test/diagnostic use only. */
+int ic_read_device_error(int clear, int* code_out);
+
+/*
+ * (a1) Activation prep + dynamic per-token INT8 quantisation, one HBM pass.
+ *
+ * Replaces Linear._prep_activation (_ops.py:337-365), rotate_activations
+ * (_quant_utils.py:117-147), the INT8 smooth divide (_ops.py:529-533) and
+ * dynamic_quantize_activation (kernels/triton_quantize.py:151-198).
+ *
+ *   x         [M, K] f16/bf16, row stride ldx              (read)
+ *   smoothrot [K] fp32 or NULL: x /= fp16(smoothrot) before the rotation
+ *   rot_size  0 (no rotation) or a power of two in [2, 4096]; powers of 4 use
+ *             the regular Hadamard kron(H4/2), others the Sylvester one
+ *   w_in      output width; the rotated row (K rounded up to rot_size) is
+ *             zero-padded to w_in (w_in >= that width)
+ *   perm      [w_in] int32 or NULL: out[:, j] = padded[:, perm[j]]
+ *   smooth    [w_in] fp32 or NULL: out /= fp16(smooth) after the gather
+ *   x_int8    [M, ldq] int8 or NULL (ldq >= w_in, ldq % 16 == 0); columns
+ *             [w_in, ldq) are written with zeros
+ *   s_a       [M] fp32 (required when x_int8 is given): max(amax,1e-8)/127
+ *   x_prep    [M, w_in] in x's dtype or NULL: the prepped activations
+ *   rowsum    [M] fp32 or NULL: sum of the prepped row (zero-point term)
+ * Quantisation is q = clamp(rint(x / s), -128, 127) with IEEE division, i.e.
+ * the CPU form kernels/triton_quantize.py:43-54 (round half to even).
+ */
+int ic_prep_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                  const float* smoothrot, int rot_size, int64_t w_in, const int32_t* perm,
+                  const float* smooth, int8_t* x_int8, int64_t ldq, float* s_a,
+                  void* x_prep, float* rowsum, void* stream);
+
+/* dynamic_quantize_activation (kernels/triton_quantize.py:151-198): the
+ * special case of ic_prep_quant with no smoothing, rotation or gather. */
+int ic_dynamic_quantize(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                        int8_t* x_int8, int64_t ldq, float* s_a, void* stream);
+
+/*
+ * (a2, a3) INT8-activation GEMM with fused dequant on tcgen05 (kind::i8):
+ *
+ *   out[m, n] = s_a[m] * sum_g s_w[n, g] * (sum_{k in g} xq[m, k] * w[n, k])
+ *               + bias[n] - rowsum[m] * zp_corr[n]
+ *
+ * Replaces fused_int8_gemm_dequant (kernels/triton_int8_gemm.py:135-205),
+ * fused_w4a8_gemm_dequant (kernels/triton_w4a8_gemm.py:111-169) together
+ * with unpack_int4_to_int8 (kernels/triton_int4_to_int8_unpack.py:55-81):
+ * INT4 weights are unpacked inside the kernel, never materialised.
+ *
+ *   xq      [M, K] int8, row stride ldq bytes (ldq % 16 == 0)
+ *   w       IC_W_INT8: int8 [N, K] (ldw % 16 == 0, K % 16 == 0)
+ *           IC_W_INT4: uint8 [N, ceil(K/2)] (ldw % 16 == 0, K % 32 == 0)
+ *   s_w     fp32 [N, G] row-major; G == 1 is per-channel, G > 1 groups of
+ *           group_size consecutive k (group_size % 128 == 0); the group form
+ *           follows _quant_utils.py:255-270
+ *   s_a     fp32 [M]
+ *   bias    [N] in bias_dtype or NULL
+ *   rowsum, zp_corr  fp32 [M], fp32 [N] or both NULL (zero-point term of
+ *           _ops.py:459-461)
+ *   out     [M, N] in out_dtype (f16/bf16/f32), row stride ldo
+ */
+int ic_gemm_a8(const int8_t* xq, int64_t M, int64_t K, int64_t ldq,
+               const void* w, int w_kind, int64_t N, int64_t ldw,
+               const float* s_w, int64_t G, int64_t group_size, const float* s_a,
+               const void* bias, int bias_dtype, const float* rowsum, const float* zp_corr,
+               void* out, int out_dtype, int64_t ldo, void* stream);
+
+/*
+ * (a4) W4A16: out = x @ dequant(w)^T with dequant(w)[n,k] = fp16(q[n,k] *
+ * s[n, k // group_size]), fp32 accumulation, fused bias and low-rank term
+ *   out = fp16(fp16(x @ W^T + bias) + lr_scale * lr_mid @ lr_up^T)
+ * (the second rounding reproduces the reference's separate addmm_).
+ *
+ * Replaces unpack_int4_to_float16 (kernels/triton_int4_unpack.py:62-88) +
+ * F.linear (_ops.py:473-474), the PyTorch INT4 path (_ops.py:483-491) and the
+ * LoRA residual (_ops.py:236-244) for standard LoRA.
+ *
+ *   x      [M, K] fp16 (x_dtype must be IC_DTYPE_F16), row stride ldx
+ *   w      uint8 [N, ceil(K/2)], row stride ldw bytes
+ *   scale  [N, G] in scale_dtype (f16 or f32; cast to fp16 like the
+ *          reference), group_size % 128 == 0 when G > 1
+ *   bias   [N] or NULL
+ *   lr_mid [M, R] fp16, lr_up [N, R] fp16 (R <= 64) or NULL
+ *   out    [M, N] fp16, row stride ldo
+ */
+int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                  const uint8_t* w, int64_t N, int64_t ldw,
+                  const void* scale, int scale_dtype, int64_t G, int64_t group_size,
+                  const void* bias, int bias_dtype,
+                  const void* lr_mid, const void* lr_up, int64_t R, float lr_scale,
+                  void* out, int64_t ldo, void* stream);
+
+/* Low-rank "down" projection mid = fp16(x @ down^T) (_ops.py:242, F.linear
+ * in fp16): x [M, K] fp16 (ldx), down [R, K] fp16, mid [M, R] fp16. */
+int ic_lowrank_down(const void* x, int64_t M, int64_t K, int64_t ldx, const void* down,
+                    int64_t R, void* mid, void* stream);
+
+/* In-place low-rank residual out = fp16(out + scale * mid @ up^T)
+ * (out.addmm_ of _ops.py:243 / :384): out [M, N] fp16 (ldo),
+ * mid [M, R] fp16, up [N, R] fp16. */
+int ic_lowrank_add(void* out, int64_t M, int64_t N, int64_t ldo, const void* mid,
+                   const void* up, int64_t R, float scale, void* stream);
+
+/* unpack_int4_to_int8 (kernels/triton_int4_to_int8_unpack.py:55-81):
+ * packed [N, ldp bytes] -> out int8 [N, K] (row stride K). */
+int ic_unpack_int4_to_int8(const uint8_t* packed, int64_t N, int64_t K, int64_t ldp,
+                           int8_t* out, void* stream);
+
+/* unpack_int4_to_float16 (kernels/triton_int4_unpack.py:62-88), extended to
+ * group scales: out[n,k] = fp16(q * fp16(scale[n, k // group_size])). */
+int ic_unpack_int4_to_f16(const uint8_t* packed, int64_t N, int64_t K, int64_t ldp,
+                          const void* scale, int scale_dtype, int64_t G, int64_t group_size,
+                          void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* INTCRUSH_B200_H_ */

@@ -1,0 +1,242 @@
+"""GPU parity of every C-ABI kernel against the CPU oracle (``oracle/``).
+
+Bars (stated per test): bit-exact for the INT8 activations, scales, prepped
+fp16 rows, unpacked weights and integer accumulators; max-rel
+``max|y - y_ref| / max|y_ref|`` <= 1e-3 for W4A16 / dequant paths and
+<= 3e-2 for the A8 paths (the tolerances of the parity contract).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import intcrush_oracle as O
+from _pkg import load
+
+pytestmark = pytest.mark.gpu
+
+rt = load("_b200_runtime")
+
+
+def _dev():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA required")
+    return torch.device("cuda")
+
+
+def _x(M, K, seed, outliers=True, dtype=np.float16):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    if outliers and K >= 10:
+        ch = rng.permutation(K)[: max(1, round(0.01 * K))]
+        x[:, ch] *= 20
+    return x.astype(dtype)
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+# ───────────────────────────── a1: prep + quant ─────────────────────────────
+
+PREP_CASES = [
+    # M, K, rot, w_in, perm, smoothrot, smooth
+    (1, 64, 0, 64, False, False, False),
+    (7, 256, 16, 256, False, False, False),
+    (16, 1024, 64, 1024, True, False, False),
+    (129, 3072, 256, 3072, True, True, False),
+    (33, 3000, 256, 3072, True, False, True),      # K pad to a rot multiple
+    (5, 3072, 1024, 3072, False, True, False),
+    (4, 3072, 4096, 4096, True, False, False),     # K=3072 padded to 4096
+    (9, 5120, 1024, 5120, False, False, True),
+    (3, 13824, 1024, 14336, True, False, False),  # 13824 pads to 14336
+    (6, 96, 32, 96, False, False, False),          # Sylvester size
+    (6, 512, 128, 512, True, True, False),         # Sylvester size
+    (2, 100, 0, 112, True, False, True),           # no rotation, pad to w_in
+]
+
+
+@pytest.mark.parametrize("M,K,rot,w_in,use_perm,use_sr,use_sm", PREP_CASES)
+def test_prep_quant_bit_exact(M, K, rot, w_in, use_perm, use_sr, use_sm):
+    dev = _dev()
+    x = _x(M, K, seed=M * 7 + K)
+    rng = np.random.default_rng(1)
+    perm = rng.permutation(w_in).astype(np.int64) if use_perm else None
+    sr = rng.uniform(0.5, 4.0, K).astype(np.float32) if use_sr else None
+    sm = rng.uniform(0.5, 2.0, w_in).astype(np.float32) if use_sm else None
+    ref = O.prep_activation(x, smoothrot=sr, rot_need=rot > 0, rot_size=rot, w_in=w_in, perm=perm,
+                            smooth=sm, int8_path=True)
+    q_ref, s_ref = O.quantize_rows(ref)
+    xq, s_a, xp, rs = rt.prep_quantize(
+        _t(x, dev), smoothrot=None if sr is None else _t(sr, dev), rot_size=rot, w_in=w_in,
+        perm=None if perm is None else _t(perm, dev), smooth=None if sm is None else _t(sm, dev),
+        want_prep=True, want_rowsum=True)
+    torch.cuda.synchronize()
+    assert np.array_equal(xp.cpu().numpy().view(np.uint16), ref.view(np.uint16)), "prepped fp16 row differs"
+    assert np.array_equal(s_a.cpu().numpy(), s_ref), "scales differ"
+    assert np.array_equal(xq.cpu().numpy(), q_ref), "int8 activations differ"
+    np.testing.assert_allclose(rs.cpu().numpy(), ref.astype(np.float64).sum(1), rtol=1e-3, atol=1e-2)
+
+
+def test_prep_bf16_runs_and_matches_fp16_semantics():
+    dev = _dev()
+    x = torch.randn(8, 256, device=dev, dtype=torch.bfloat16)
+    xq, s_a, xp, _ = rt.prep_quantize(x, rot_size=64, want_prep=True)
+    H = torch.from_numpy(O.hadamard(64)).to(dev)
+    ref = (x.double().reshape(8, 4, 64) @ H.T).reshape(8, 256).to(torch.bfloat16)
+    assert torch.equal(xp, ref)
+
+
+def test_dynamic_quantize_matches_reference_cpu_formula():
+    """Mirror of the reference's ``test_cpu_fallback`` cases, on the GPU."""
+    dev = _dev()
+    for M, K in [(1, 64), (4, 256), (16, 1024), (256, 4096)]:
+        torch.manual_seed(0)
+        x = torch.randn(M, K).half()
+        q, s = rt.dynamic_quantize_activation(x.to(dev))
+        ref_s = x.float().abs().amax(dim=1).clamp(min=1e-8) / 127.0
+        ref_q = (x.float() / ref_s.unsqueeze(1)).round().clamp(-128, 127).to(torch.int8)
+        assert torch.equal(q.cpu(), ref_q)
+        assert torch.equal(s.cpu(), ref_s)
+
+
+def test_dynamic_quantize_3d_and_zero_rows():
+    dev = _dev()
+    x = torch.zeros(2, 3, 128, dtype=torch.float16, device=dev)
+    x[1, 2, 5] = 3.0
+    q, s = rt.dynamic_quantize_activation(x)
+    assert q.shape == (2, 3, 128) and s.shape == (2, 3)
+    assert int(q.abs().sum()) == 127
+    assert torch.all(s[0] == torch.tensor(1e-8, dtype=torch.float32) / 127.0)
+
+
+# ───────────────────────────── a2/a3: A8 GEMMs ──────────────────────────────
+
+def _int_inputs(M, N, K, seed, int4):
+    rng = np.random.default_rng(seed)
+    xq = rng.integers(-128, 128, (M, K), dtype=np.int64).astype(np.int8)
+    if int4:
+        wq = rng.integers(-8, 8, (N, K), dtype=np.int64).astype(np.int8)
+    else:
+        wq = rng.integers(-127, 128, (N, K), dtype=np.int64).astype(np.int8)
+    return xq, wq
+
+
+@pytest.mark.parametrize("int4", [False, True])
+@pytest.mark.parametrize("G", [1, 4])
+@pytest.mark.parametrize("M,N,K", [(1, 128, 512), (37, 200, 512), (130, 384, 1024), (300, 256, 512)])
+def test_gemm_a8_integer_accumulators_exact(int4, G, M, N, K):
+    """With unit scales the output is the int32 accumulator (sum over groups):
+    exact in fp32 below 2^24."""
+    dev = _dev()
+    if G > 1 and not int4 and K // G != 128:
+        G = K // 128
+    xq, wq = _int_inputs(M, N, K, seed=M + N + K, int4=int4)
+    w = O.pack_int4(wq) if int4 else wq
+    s_w = np.ones((N, G), np.float32)
+    s_a = np.ones(M, np.float32)
+    out = rt.gemm_a8(_t(xq, dev), _t(w, dev), _t(s_w, dev), _t(s_a, dev), out_dtype=torch.float32,
+                     group_size=K // G)
+    ref = O.int_accumulators(xq, wq)[0]
+    assert np.array_equal(out.cpu().numpy().astype(np.int64), ref)
+
+
+@pytest.mark.parametrize("int4,G", [(False, 1), (True, 1), (True, 24), (False, 24)])
+@pytest.mark.parametrize("M", [1, 16, 64, 129, 256, 520])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
+def test_gemm_a8_dequant_parity(int4, G, M, out_dtype):
+    dev = _dev()
+    N, K = 384, 3072
+    xq, wq = _int_inputs(M, N, K, seed=M, int4=int4)
+    rng = np.random.default_rng(M + 1)
+    s_w = rng.uniform(1e-3, 2e-2, (N, G)).astype(np.float32)
+    s_a = rng.uniform(1e-3, 5e-2, M).astype(np.float32)
+    bias = (rng.standard_normal(N) * 0.02).astype(np.float16)
+    w = O.pack_int4(wq) if int4 else wq
+    out = rt.gemm_a8(_t(xq, dev), _t(w, dev), _t(s_w, dev), _t(s_a, dev), bias=_t(bias, dev),
+                     out_dtype=out_dtype, group_size=K // G)
+    ref = O.gemm_a8(xq, s_a, wq, s_w if G > 1 else s_w[:, 0], bias=bias, group_size=K // G)
+    assert O.max_rel(out.float().cpu().numpy(), ref) <= 3e-2
+    # fp32 accumulation makes it far tighter than the contract
+    assert O.max_rel(out.float().cpu().numpy(), ref) <= 5e-3
+
+
+def test_gemm_a8_zero_point_term():
+    dev = _dev()
+    M, N, K = 40, 256, 512
+    xq, wq = _int_inputs(M, N, K, seed=3, int4=False)
+    rng = np.random.default_rng(4)
+    s_w = rng.uniform(1e-3, 2e-2, N).astype(np.float32)
+    s_a = rng.uniform(1e-3, 5e-2, M).astype(np.float32)
+    rowsum = rng.standard_normal(M).astype(np.float32)
+    zpc = rng.standard_normal(N).astype(np.float32) * 0.01
+    out = rt.gemm_a8(_t(xq, dev), _t(wq, dev), _t(s_w, dev), _t(s_a, dev), out_dtype=torch.float32,
+                     rowsum=_t(rowsum, dev), zp_corr=_t(zpc, dev))
+    ref = O.gemm_a8(xq, s_a, wq, s_w) - rowsum[:, None].astype(np.float64) * zpc[None, :]
+    assert O.max_rel(out.cpu().numpy(), ref) <= 1e-5
+
+
+def test_gemm_a8_unpacked_int4_matches_packed():
+    dev = _dev()
+    M, N, K = 64, 256, 1024
+    xq, wq = _int_inputs(M, N, K, seed=9, int4=True)
+    s_w = np.full((N, 8), 0.01, np.float32)
+    s_a = np.full(M, 0.02, np.float32)
+    a = rt.gemm_a8(_t(xq, dev), _t(wq, dev), _t(s_w, dev), _t(s_a, dev), out_dtype=torch.float32)
+    b = rt.gemm_a8(_t(xq, dev), _t(O.pack_int4(wq), dev), _t(s_w, dev), _t(s_a, dev), out_dtype=torch.float32)
+    assert torch.equal(a, b)
+
+
+# ───────────────────────────── a4: W4A16 ────────────────────────────────────
+
+@pytest.mark.parametrize("M", [1, 5, 16, 32, 33, 64, 256])
+@pytest.mark.parametrize("G", [1, 24])
+def test_w4a16_parity(M, G):
+    dev = _dev()
+    N, K = 3072, 3072
+    rng = np.random.default_rng(M * 3 + G)
+    x = (rng.standard_normal((M, K))).astype(np.float16)
+    q = rng.integers(-8, 8, (N, K)).astype(np.int8)
+    packed = O.pack_int4(q)
+    scale = rng.uniform(1e-3, 2e-2, (N, G)).astype(np.float16)
+    out = rt.gemm_w4a16(_t(x, dev), _t(packed, dev), _t(scale, dev), group_size=K // G)
+    w16 = O.dequant_int4_f16(packed, scale, K, K // G)
+    ref = O.linear_f16(x, w16)
+    assert O.max_rel(out.float().cpu().numpy(), ref) <= 1e-3
+
+
+@pytest.mark.parametrize("M", [1, 16, 256])
+def test_w4a16_with_lora_parity(M):
+    dev = _dev()
+    N, K, R = 3072, 3072, 32
+    rng = np.random.default_rng(M)
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    q = rng.integers(-8, 8, (N, K)).astype(np.int8)
+    packed = O.pack_int4(q)
+    scale = rng.uniform(1e-3, 2e-2, (N, 24)).astype(np.float16)
+    A = (rng.standard_normal((R, K)) * 0.01).astype(np.float16)
+    B = (rng.standard_normal((N, R)) * 0.01).astype(np.float16)
+    mid = rt.lowrank_down(_t(x, dev), _t(A, dev))
+    assert np.array_equal(mid.cpu().numpy(), O.lora_mid(x, A)) or \
+        np.abs(mid.float().cpu().numpy() - O.lora_mid(x, A).astype(np.float32)).max() <= 2e-3
+    out = rt.gemm_w4a16(_t(x, dev), _t(packed, dev), _t(scale, dev), group_size=128,
+                        lr_mid=mid, lr_up=_t(B, dev), lr_scale=1.0)
+    ref = O.linear_f16(x, O.dequant_int4_f16(packed, scale, K, 128)) + O.lora_residual(x, A, B, 1.0)
+    assert O.max_rel(out.float().cpu().numpy(), ref) <= 1e-3
+
+
+def test_unpack_kernels_bit_exact():
+    dev = _dev()
+    rng = np.random.default_rng(0)
+    q = rng.integers(-8, 8, (16, 256)).astype(np.int8)
+    packed = O.pack_int4(q)
+    got = rt.unpack_int4_to_int8(_t(packed, dev), 256)
+    assert np.array_equal(got.cpu().numpy(), q)
+    scale = rng.uniform(1e-3, 2e-2, (16, 2)).astype(np.float16)
+    w16 = rt.unpack_int4_to_float16(_t(packed, dev), _t(scale, dev), 256, group_size=128)
+    assert np.array_equal(w16.cpu().numpy().view(np.uint16), O.dequant_int4_f16(packed, scale, 256, 128).view(np.uint16))
+
+
+def test_no_device_timeouts_recorded():
+    _dev()
+    assert rt.device_error(clear=True) == 0
