@@ -1,0 +1,303 @@
+"""Benchmark of the quantized-linear forward path on B200.
+
+Workload: one INT4 W4A8 linear
+  x fp16 [4096, 3072] ~N(0,1) with 1% outlier channels x20, SmoothRot factors
+  U[0.5, 4], rot_size 256, PermuQuant perm = randperm(3072), weights INT4
+  U[-8, 7] packed [12288, 1536], group-128 scales U[1e-3, 2e-2].
+A step = the whole forward of that layer: prep + per-token INT8 quant (one
+kernel) and the group-scale W4A8 GEMM with bias (one kernel).
+Metric: linear TOPS = 2*M*N*K / step time (higher is better).
+
+* ``value``: device time of the steps (CUDA events per step, L2 flushed by a
+  256 MB write between steps, outside the timed events), whole job over all
+  ranks (weak scaling: every rank runs its own 4096 tokens; no collective).
+* ``e2e``: the same step through the runtime API with the input copied from
+  pinned host memory and the output copied back to pinned host memory inside
+  the timed region.
+* ``roofline``: the GEMM kernel's algorithmic ops / its event time against the
+  dense INT8 peak (2 x the measured bf16 cuBLAS figure); prep against HBM.
+* ``cpu_baseline``: the reference's PyTorch CPU path (torch restatement,
+  oracle/torch_reference_path.py) on a 256-token sample of the same layer.
+
+``--impl reference`` times that CPU path alone (all host threads), printing
+the same metric.  Under torchrun only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+import types
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = "comfyui-int-crush_b200"
+M, K, N, GS, ROT = 4096, 3072, 12288, 128, 256
+OPS = 2.0 * M * N * K
+
+
+def _pkg():
+    if PKG not in sys.modules:
+        m = types.ModuleType(PKG)
+        m.__path__ = [os.path.join(ROOT, PKG)]
+        m.__package__ = PKG
+        sys.modules[PKG] = m
+    import importlib
+    return importlib.import_module(PKG + "._b200_runtime")
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def make_inputs(seed: int = 0, device="cpu"):
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, K, generator=g)
+    ch = torch.randperm(K, generator=g)[: round(0.01 * K)]
+    x[:, ch] *= 20
+    x = x.half()
+    smoothrot = (torch.rand(K, generator=g) * 3.5 + 0.5).half().float()
+    perm = torch.randperm(K, generator=g)
+    q = torch.randint(-8, 8, (N, K), generator=g, dtype=torch.int8)
+    qu = (q.to(torch.int16) & 0xF).to(torch.uint8)
+    packed = (qu[:, 0::2] | (qu[:, 1::2] << 4)).contiguous()
+    scale = (torch.rand(N, K // GS, generator=g) * (2e-2 - 1e-3) + 1e-3).half()
+    bias = (torch.randn(N, generator=g) * 0.02).half()
+    d = dict(x=x, smoothrot=smoothrot, perm=perm, packed=packed, scale=scale, bias=bias)
+    return {k: v.to(device) for k, v in d.items()}
+
+
+# ───────────────────────────── CPU baseline ─────────────────────────────────
+
+def cpu_baseline(sample_rows: int = 256, reps: int = 3, threads: int | None = None):
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import torch_reference_path as TR
+    if threads:
+        torch.set_num_threads(threads)
+    d = make_inputs()
+    xs = d["x"][:sample_rows]
+    times = []
+    for i in range(reps + 1):
+        t0 = time.perf_counter()
+        TR.forward_int4_pytorch(xs, d["packed"], d["scale"], K, GS, smoothrot=d["smoothrot"],
+                                rot_size=ROT, w_in=K, perm=d["perm"])
+        dt = time.perf_counter() - t0
+        if i:
+            times.append(dt)
+    times.sort()
+    t = times[len(times) // 2]
+    tops = 2.0 * sample_rows * N * K / t / 1e12
+    return {"value": tops, "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{sample_rows} of {M} tokens of the config-2 layer, torch CPU fp16 "
+                      f"(dequant group-128 + F.linear + prep), median of {reps}, {t * 1e3:.1f} ms"}
+
+
+def run_reference(args, rank: int) -> None:
+    if rank != 0:
+        return
+    import torch
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    for _ in range(max(args.warmup, 1)):
+        cpu_baseline(64, reps=1)
+    steps = []
+    for _ in range(args.steps):
+        r = cpu_baseline(256, reps=1)
+        steps.append(r["value"])
+    v = sorted(steps)[len(steps) // 2]
+    ms = 2.0 * M * N * K / (v * 1e12) * 1e3
+    line = {"metric": "w4a8_linear_tops", "value": v, "unit": "TOPS", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "config2_w4a8_linear M4096 K3072 N12288 g128 rot256 perm smoothrot",
+                       "sample_tokens": 256},
+            "cpu_baseline": {"value": v, "unit": "TOPS", "cores": threads, "kind": "port",
+                             "sample": "256 of 4096 tokens per step, torch CPU path of the reference"},
+            "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ───────────────────────────── GPU arm ──────────────────────────────────────
+
+class Clocks:
+    """Samples nvidia-smi during the timed region."""
+
+    def __init__(self, idx: int):
+        self.idx = idx
+        self.proc = None
+        self.path = os.path.join("/tmp", f"ic_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), "--query-gpu=clocks.sm,clocks.max.sm,power.draw,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        try:
+            rows = [r.split(",") for r in open(self.path).read().strip().splitlines() if r.strip()]
+            sm = sorted(float(r[0]) for r in rows)
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[3 + i]})
+            return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": float(rows[0][1]), "reasons": reasons,
+                    "samples": len(rows)}
+        except Exception as e:  # pragma: no cover
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": str(e)}
+
+
+def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
+    import torch
+    import torch.distributed as dist
+    rt = _pkg()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    d = make_inputs(seed=rank, device=dev)
+    s_w = d["scale"].float()
+    perm32 = d["perm"].to(torch.int32)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    st = torch.cuda.current_stream()
+
+    def step(x):
+        xq, s_a, _, _ = rt.prep_quantize(x, smoothrot=d["smoothrot"], rot_size=ROT, w_in=K, perm=perm32)
+        return rt.gemm_a8(xq, d["packed"], s_w, s_a, bias=d["bias"], out_dtype=torch.float16, group_size=GS)
+
+    for _ in range(args.warmup):
+        step(d["x"])
+    torch.cuda.synchronize()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local_rank) as clk:
+        t_wall = time.perf_counter()
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            ev[i][0].record(st)
+            xq, s_a, _, _ = rt.prep_quantize(d["x"], smoothrot=d["smoothrot"], rot_size=ROT, w_in=K, perm=perm32)
+            ev[i][1].record(st)
+            rt.gemm_a8(xq, d["packed"], s_w, s_a, bias=d["bias"], out_dtype=torch.float16, group_size=GS)
+            ev[i][2].record(st)
+        torch.cuda.synchronize()
+        t_wall = time.perf_counter() - t_wall
+    if world > 1:
+        dist.barrier()
+    prep_ms = [ev[i][0].elapsed_time(ev[i][1]) for i in range(args.steps)]
+    gemm_ms = [ev[i][1].elapsed_time(ev[i][2]) for i in range(args.steps)]
+    tot_ms = sum(prep_ms) + sum(gemm_ms)
+
+    # e2e: host-pinned input in, host-pinned output out, through the runtime API
+    x_host = d["x"].cpu().pin_memory()
+    out_host = torch.empty((M, N), dtype=torch.float16).pin_memory()
+    for _ in range(2):
+        out_host.copy_(step(x_host.to(dev, non_blocking=True)), non_blocking=True)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    e0.record(st)
+    for _ in range(args.steps):
+        xd = x_host.to(dev, non_blocking=True)
+        out_host.copy_(step(xd), non_blocking=True)
+    e1.record(st)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+
+    vals = torch.tensor([tot_ms, e2e_ms, sum(gemm_ms), sum(prep_ms)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    tot_ms, e2e_ms, gemm_sum, prep_sum = vals.tolist()
+
+    if rank != 0:
+        return
+    hbm, bf16, src = _peaks()
+    int8_peak = 2.0 * bf16
+    ms_step = tot_ms / args.steps
+    gemm_avg = gemm_sum / args.steps
+    prep_avg = prep_sum / args.steps
+    gemm_tops = OPS / (gemm_avg * 1e-3) / 1e12
+    prep_bytes = M * K * 2 + M * K * 1 + M * 4 + K * 4 * 2    # x in, int8 out, s_a, perm+smoothrot
+    prep_gbs = prep_bytes / (prep_avg * 1e-3) / 1e9
+    line = {
+        "metric": "w4a8_linear_tops", "value": world * OPS / (ms_step * 1e-3) / 1e12, "unit": "TOPS",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic",
+        "config": {"workload": "config2_w4a8_linear M4096 K3072 N12288 g128 rot256 perm smoothrot bias",
+                   "tokens_per_gpu": M, "parallelism": f"token-sharded dp{world} (no collective)",
+                   "l2": "flushed (256 MB write) between timed steps"},
+        "e2e": {"value": world * OPS * args.steps / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
+                "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
+        "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak, "unit": "TOPS",
+                     "frac": gemm_tops / int8_peak, "traffic": None,
+                     "kernel": "gemm_tc_kernel<W_I4, grouped>",
+                     "peak_source": f"2 x {src} bf16 cuBLAS ({bf16} TF/s), burst",
+                     "kernel_ms": gemm_avg},
+        "prep_roofline": {"bound": "hbm", "achieved": prep_gbs, "peak": hbm, "unit": "GB/s",
+                          "frac": prep_gbs / hbm, "kernel_ms": prep_avg, "peak_source": src},
+        "gpu_launches": 2 * args.steps,
+        "wall_ms": t_wall * 1e3,
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline()
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    try:
+        run_gpu(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
