@@ -164,7 +164,7 @@ class Clocks:
             rows = [r.split(",") for r in open(self.path).read().strip().splitlines() if r.strip()]
             sm = sorted(float(r[0]) for r in rows)
             names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-            reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[3 + i]})
+            reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].strip() == "Active"})
             return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": float(rows[0][1]), "reasons": reasons,
                     "samples": len(rows)}
         except Exception as e:  # pragma: no cover

@@ -196,6 +196,7 @@ def gemm_a8(
     group_size: int | None = None,
     rowsum: torch.Tensor | None = None,
     zp_corr: torch.Tensor | None = None,
+    repacked: bool = False,
 ) -> torch.Tensor:
     """``out = s_a[m] * sum_g s_w[n,g] * (xq @ w^T)_g + bias - rowsum (x) zp_corr``.
 
@@ -215,7 +216,7 @@ def gemm_a8(
         if w.shape[1] != K:
             raise AssertionError(f"K mismatch: {K} vs {w.shape[1]}")
     elif w.dtype == torch.uint8:
-        kind = L.IC_W_INT4
+        kind = L.IC_W_INT4R if repacked else L.IC_W_INT4
         N = w.shape[0]
         if w.shape[1] != (K + 1) // 2:
             raise AssertionError(f"packed K mismatch: {K} vs {w.shape[1]} bytes")
@@ -310,6 +311,7 @@ def gemm_w4a16(
     lr_scale: float = 1.0,
     out: torch.Tensor | None = None,
     K: int | None = None,
+    w_layout: int = 0,
 ) -> torch.Tensor:
     """W4A16: ``fp16(x @ fp16(q * s)^T (+ bias))`` then ``+= lr_scale * lr_mid @ lr_up^T``.
 
@@ -338,7 +340,8 @@ def gemm_w4a16(
     up = None if lr_up is None else lr_up.to(torch.float16).contiguous()
     R = 0 if mid is None else mid.shape[1]
     st = L.lib().ic_gemm_w4a16(
-        _p(x2), L.IC_DTYPE_F16, M, K, x2.stride(0), _p(packed), N, packed.stride(0), _p(sc), _DT[sc.dtype],
+        _p(x2), L.IC_DTYPE_F16, M, K, x2.stride(0), _p(packed), N, packed.stride(0), int(w_layout),
+        _p(sc), _DT[sc.dtype],
         G, gs, _p(b), _DT[b.dtype] if b is not None else 0, _p(mid), _p(up), R, float(lr_scale),
         _p(out), out.stride(0), _stream(x2))
     L.check(st, "ic_gemm_w4a16")
@@ -370,6 +373,18 @@ def lowrank_add(out: torch.Tensor, mid: torch.Tensor, up: torch.Tensor, scale: f
     M, N = out.shape
     L.check(L.lib().ic_lowrank_add(_p(out), M, N, out.stride(0), _p(m), _p(u), m.shape[1], float(scale),
                                    _stream(out)), "ic_lowrank_add")
+    return out
+
+
+def repack_int4(packed: torch.Tensor, K: int, layout: int) -> torch.Tensor:
+    """Load-time nibble permutation of packed INT4 weights (``ic_repack_int4``):
+    layout 0 feeds ``gemm_a8(..., repacked=True)``, layout 1 feeds
+    ``gemm_w4a16(..., w_layout=1)``.  Same shape and size as the input."""
+    _need_cuda("repack_int4", packed)
+    p = packed.contiguous()
+    out = torch.empty_like(p)
+    L.check(L.lib().ic_repack_int4(_p(p), p.shape[0], K, p.stride(0), _p(out), out.stride(0), int(layout),
+                                   _stream(p)), "ic_repack_int4")
     return out
 
 
@@ -414,5 +429,5 @@ __all__ = [
     "B200_AVAILABLE", "B200_LIBRARY_LOADED",
     "dynamic_quantize_activation", "fused_int8_gemm_dequant", "fused_quant_int8_gemm_dequant",
     "fused_w4a8_gemm_dequant", "unpack_int4_to_int8", "unpack_int4_to_float16",
-    "prep_quantize", "gemm_a8", "gemm_w4a16", "lowrank_down", "lowrank_add", "device_error",
+    "prep_quantize", "gemm_a8", "gemm_w4a16", "repack_int4", "lowrank_down", "lowrank_add", "device_error",
 ]

@@ -25,6 +25,7 @@ IC_DTYPE_F32 = 2
 
 IC_W_INT8 = 0
 IC_W_INT4 = 1
+IC_W_INT4R = 2
 
 IC_DEV_ERR_TIMEOUT = 1
 
@@ -41,7 +42,8 @@ SIGNATURES: dict[str, list] = {
     "ic_prep_quant": [_P, _I, _L, _L, _L, _P, _I, _L, _P, _P, _P, _L, _P, _P, _P, _P],
     "ic_dynamic_quantize": [_P, _I, _L, _L, _L, _P, _L, _P, _P],
     "ic_gemm_a8": [_P, _L, _L, _L, _P, _I, _L, _L, _P, _L, _L, _P, _P, _I, _P, _P, _P, _I, _L, _P],
-    "ic_gemm_w4a16": [_P, _I, _L, _L, _L, _P, _L, _L, _P, _I, _L, _L, _P, _I, _P, _P, _L, _F, _P, _L, _P],
+    "ic_gemm_w4a16": [_P, _I, _L, _L, _L, _P, _L, _L, _I, _P, _I, _L, _L, _P, _I, _P, _P, _L, _F, _P, _L, _P],
+    "ic_repack_int4": [_P, _L, _L, _L, _P, _L, _I, _P],
     "ic_lowrank_down": [_P, _L, _L, _L, _P, _L, _P, _P],
     "ic_lowrank_add": [_P, _L, _L, _L, _P, _P, _L, _F, _P],
     "ic_unpack_int4_to_int8": [_P, _L, _L, _L, _P, _P],

@@ -105,14 +105,14 @@ int ic_gemm_a8(const int8_t* xq, int64_t M, int64_t K, int64_t ldq, const void* 
   if (M < 0 || N < 0 || K <= 0) return fail(IC_ERR_ARG, "ic_gemm_a8: bad M/N/K");
   if (M == 0 || N == 0) return IC_OK;
   if (!xq || !w || !s_w || !s_a || !out) return fail(IC_ERR_ARG, "ic_gemm_a8: NULL operand");
-  if (w_kind != IC_W_INT8 && w_kind != IC_W_INT4) return fail(IC_ERR_ARG, "ic_gemm_a8: bad w_kind");
+  if (w_kind != IC_W_INT8 && w_kind != IC_W_INT4 && w_kind != IC_W_INT4R) return fail(IC_ERR_ARG, "ic_gemm_a8: bad w_kind");
   if (out_dtype < IC_DTYPE_F16 || out_dtype > IC_DTYPE_F32) return fail(IC_ERR_ARG, "ic_gemm_a8: bad out dtype");
   if (bias && (bias_dtype < IC_DTYPE_F16 || bias_dtype > IC_DTYPE_F32)) return fail(IC_ERR_ARG, "ic_gemm_a8: bad bias dtype");
   if ((rowsum == nullptr) != (zp_corr == nullptr)) return fail(IC_ERR_ARG, "ic_gemm_a8: rowsum and zp_corr go together");
   if (ldq < K || ldq % 16 || !aligned16(xq)) return fail(IC_ERR_ARG, "ic_gemm_a8: xq needs ldq >= K, ldq %% 16 == 0, 16-byte alignment");
   if (!aligned16(w) || ldw % 16) return fail(IC_ERR_ARG, "ic_gemm_a8: weights need 16-byte aligned base and row stride");
   if (w_kind == IC_W_INT8 && (K % 16 || ldw < K)) return fail(IC_ERR_ARG, "ic_gemm_a8: int8 weights need K %% 16 == 0 and ldw >= K");
-  if (w_kind == IC_W_INT4 && (K % 32 || ldw < K / 2)) return fail(IC_ERR_ARG, "ic_gemm_a8: int4 weights need K %% 32 == 0 and ldw >= K/2");
+  if (w_kind != IC_W_INT8 && (K % 32 || ldw < K / 2)) return fail(IC_ERR_ARG, "ic_gemm_a8: int4 weights need K %% 32 == 0 and ldw >= K/2");
   if (ldo < N) return fail(IC_ERR_ARG, "ic_gemm_a8: ldo < N");
   if (G < 1) return fail(IC_ERR_ARG, "ic_gemm_a8: G must be >= 1");
   if (G > 1) {
@@ -127,15 +127,16 @@ int ic_gemm_a8(const int8_t* xq, int64_t M, int64_t K, int64_t ldq, const void* 
   a.G = (int)G; a.kb_per_group = G > 1 ? (int)(group_size / 128) : 0; a.group_size = (int)group_size;
   a.s_w = s_w; a.s_a = s_a; a.bias = bias; a.bias_dtype = bias_dtype; a.rowsum = rowsum; a.zp_corr = zp_corr;
   a.out = out; a.out_dtype = out_dtype; a.ldo = ldo;
+  a.w_repacked = (w_kind == IC_W_INT4R);
   const char* why = "kernel launch";
   const int force_bn = 0;
-  cudaError_t e = ic::launch_gemm_a8(xq, (int)M, (int)K, ldq, w, w_kind, (int)N, ldw, a, force_bn,
+  cudaError_t e = ic::launch_gemm_a8(xq, (int)M, (int)K, ldq, w, w_kind == IC_W_INT8 ? IC_W_INT8 : IC_W_INT4, (int)N, ldw, a, force_bn,
                                      (cudaStream_t)stream, &why);
   return cuda_status(e, why);
 }
 
 int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const uint8_t* w, int64_t N,
-                  int64_t ldw, const void* scale, int scale_dtype, int64_t G, int64_t group_size,
+                  int64_t ldw, int w_layout, const void* scale, int scale_dtype, int64_t G, int64_t group_size,
                   const void* bias, int bias_dtype, const void* lr_mid, const void* lr_up, int64_t R,
                   float lr_scale, void* out, int64_t ldo, void* stream) {
   g_err[0] = 0;
@@ -148,6 +149,7 @@ int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
   if (G > 1 && (group_size <= 0 || group_size % 128 || (K + group_size - 1) / group_size != G))
     return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: group_size must be a multiple of 128 with G == ceil(K/group_size)");
   if (ldw < (K + 1) / 2) return fail(IC_ERR_ARG, "ic_gemm_w4a16: ldw < ceil(K/2)");
+  if (w_layout != 0 && w_layout != 1) return fail(IC_ERR_ARG, "ic_gemm_w4a16: w_layout must be 0 or 1");
   if ((lr_mid == nullptr) != (lr_up == nullptr)) return fail(IC_ERR_ARG, "ic_gemm_w4a16: lr_mid and lr_up go together");
   if (lr_mid && (R <= 0 || R > 64)) return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: low-rank R must be in [1, 64]");
   const cudaStream_t st = (cudaStream_t)stream;
@@ -156,7 +158,7 @@ int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
     s.x = (const __half*)x; s.M = (int)M; s.K = (int)K; s.ldx = ldx; s.w = w; s.N = (int)N; s.ldw = ldw;
     s.scale = scale; s.scale_dtype = scale_dtype; s.G = (int)G; s.group_size = (int)group_size;
     s.bias = bias; s.bias_dtype = bias_dtype; s.lr_mid = (const __half*)lr_mid; s.lr_up = (const __half*)lr_up;
-    s.R = (int)R; s.lr_scale = lr_scale; s.out = (__half*)out; s.ldo = ldo;
+    s.R = (int)R; s.lr_scale = lr_scale; s.out = (__half*)out; s.ldo = ldo; s.repacked = w_layout;
     return cuda_status(ic::launch_w4a16_skinny(s, st), "ic_gemm_w4a16 (small M) launch");
   }
   if (K % 64 || ldx % 8 || !aligned16(x) || ldw % 16 || !aligned16(w))
@@ -165,6 +167,7 @@ int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
   memset(&a, 0, sizeof(a));
   a.G = (int)G; a.group_size = (int)group_size; a.w_scale = scale; a.w_scale_dtype = scale_dtype;
   a.bias = bias; a.bias_dtype = bias_dtype; a.out = out; a.out_dtype = IC_DTYPE_F16; a.ldo = ldo;
+  a.w_repacked = w_layout;
   const char* why = "kernel launch";
   cudaError_t e = ic::launch_gemm_w4a16_tc(x, (int)M, (int)K, ldx, w, (int)N, ldw, a, 0, st, &why);
   if (e != cudaSuccess) return cuda_status(e, why);
@@ -196,6 +199,19 @@ int ic_lowrank_add(void* out, int64_t M, int64_t N, int64_t ldo, const void* mid
   return cuda_status(ic::launch_lowrank_add((__half*)out, (int)M, (int)N, ldo, (const __half*)mid,
                                             (const __half*)up, (int)R, scale, (cudaStream_t)stream),
                      "ic_lowrank_add launch");
+}
+
+int ic_repack_int4(const uint8_t* src, int64_t N, int64_t K, int64_t lds, uint8_t* dst, int64_t ldd, int layout,
+                   void* stream) {
+  g_err[0] = 0;
+  if (N < 0 || K < 0 || lds < (K + 1) / 2 || ldd < (K + 1) / 2) return fail(IC_ERR_ARG, "ic_repack_int4: bad sizes");
+  if (layout != 0 && layout != 1) return fail(IC_ERR_ARG, "ic_repack_int4: layout must be 0 or 1");
+  if (N == 0 || K == 0) return IC_OK;
+  if (!src || !dst) return fail(IC_ERR_ARG, "ic_repack_int4: NULL operand");
+  const uintptr_t s0 = (uintptr_t)src, s1 = s0 + (uintptr_t)(N * lds), d0 = (uintptr_t)dst, d1 = d0 + (uintptr_t)(N * ldd);
+  if (s0 < d1 && d0 < s1) return fail(IC_ERR_ARG, "ic_repack_int4: src and dst overlap");
+  return cuda_status(ic::launch_repack(src, (int)N, (int)K, lds, dst, ldd, layout, (cudaStream_t)stream),
+                     "ic_repack_int4 launch");
 }
 
 int ic_unpack_int4_to_int8(const uint8_t* packed, int64_t N, int64_t K, int64_t ldp, int8_t* out, void* stream) {

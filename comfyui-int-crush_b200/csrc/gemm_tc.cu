@@ -36,6 +36,8 @@
 // expansion, 4.. = epilogue (4 or 8 warps).  Every wait is bounded.
 #include "ic_common.cuh"
 
+#include <type_traits>
+
 namespace ic {
 
 enum WMode : int { W_I8 = 0, W_I4 = 1, W_I4F = 2 };
@@ -52,6 +54,7 @@ struct GemmArgs {
   const void* w_scale;      // W_I4F: [N, G] f16/f32
   int w_scale_dtype;
   int group_size;
+  int w_repacked;           // INT4 weights in the expansion-friendly layout (ic_repack_int4)
   const float* s_a;         // [M]
   const void* bias;
   int bias_dtype;
@@ -66,31 +69,47 @@ constexpr int kTileN = 128;            // weight rows per tile (UMMA M)
 constexpr uint32_t kMagic = 0x4B400000u;
 constexpr float kMagicF = 12582912.0f; // 1.5 * 2^23
 
+// Shared-memory plan.  W_I8: one ring whose stages hold the weight tile and
+// the activation tile (both by TMA).  W_I4 / W_I4F: three rings -- the packed
+// weight tiles (P, by TMA, deep), the expanded weight tiles (W, written by the
+// expansion warps) and the activation tiles (X, by TMA) -- so that the TMA
+// latency of the packed stream is hidden independently of the MMA ring.
 template <int MODE, int BN, bool GROUPED>
 struct Cfg {
-  static constexpr int EPI = (BN > 128) ? 8 : 4;                 // epilogue warps
+  static constexpr bool I4 = (MODE != W_I8);
+  // epilogue warps: group-scaled tiles keep 64 fp32 accumulators per thread
+  // (one warp per 32 TMEM lanes x 64 columns); per-channel tiles stream.
+  static constexpr int EPI = GROUPED ? (BN >= 64 ? BN / 16 : 4) : ((BN > 128) ? 8 : 4);
   static constexpr int CPT = BN / (EPI / 4);                      // columns per epilogue thread
   static constexpr int THREADS = 32 * (4 + EPI);
   static constexpr int W_BYTES = kTileN * 128;                    // 16 KB
   static constexpr int X_BYTES = BN * 128;
   static constexpr int P_BYTES = (MODE == W_I4) ? kTileN * 64 : (MODE == W_I4F ? kTileN * 32 : 0);
-  static constexpr int STAGE_BYTES = W_BYTES + X_BYTES + P_BYTES;
-  static constexpr int STAGES_RAW = (220 * 1024) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_RAW > 6 ? 6 : STAGES_RAW;
+  static constexpr int BUDGET = 224 * 1024;
+  static constexpr int S_P = I4 ? 8 : 0;   // even: the two expansion warps own alternate stages
+  static constexpr int S_W = I4 ? 4 : 0;
+  static constexpr int XSTAGE = I4 ? X_BYTES : (X_BYTES + W_BYTES);
+  static constexpr int S_X_RAW = (BUDGET - S_P * P_BYTES - S_W * W_BYTES) / XSTAGE;
+  static constexpr int S_X = S_X_RAW > 6 ? 6 : S_X_RAW;
+  static constexpr int OFF_W = S_X * XSTAGE;                      // W ring (I4)
+  static constexpr int OFF_P = OFF_W + S_W * W_BYTES;             // P ring (I4)
+  static constexpr int OFF_BAR = OFF_P + S_P * P_BYTES;
   static constexpr int TMEM_COLS_RAW = 2 * BN;
   static constexpr int TMEM_COLS = TMEM_COLS_RAW <= 32 ? 32 : TMEM_COLS_RAW <= 64 ? 64
                                  : TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
-  static constexpr int BAR_BYTES = 1024;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;   // + alignment slack
-  static constexpr int KB_ELEMS = (MODE == W_I4F) ? 64 : 128;           // K elements per block
+  static constexpr int SMEM = OFF_BAR + 512 + 1024;               // barriers + alignment slack
+  static constexpr int KB_ELEMS = (MODE == W_I4F) ? 64 : 128;     // K elements per block
+  static_assert(EPI % 4 == 0, "epilogue warps cover the four TMEM lane quarters evenly");
   static_assert(CPT % 32 == 0, "epilogue columns per thread must be a multiple of 32");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
-  static_assert(STAGES >= 2, "pipeline depth");
+  static_assert(S_X >= 2, "pipeline depth");
   static_assert(!(GROUPED && MODE == W_I4F), "W4A16 folds scales into the weights");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
 // Nibble pairs -> int8 bytes holding 16*q (two's complement nibble in the
-// high half of each byte).  Input word: 8 nibbles, k = 0..7 from the low end.
+// high half of each byte).  Reference packing: 8 nibbles, k = 0..7 from the
+// low end.
 __device__ __forceinline__ void expand_i4_i8(uint32_t v, uint32_t& o0, uint32_t& o1) {
   const uint32_t lo = (v << 4) & 0xF0F0F0F0u;   // even k
   const uint32_t hi = v & 0xF0F0F0F0u;          // odd k
@@ -109,6 +128,77 @@ __device__ __forceinline__ uint32_t expand_i4_f16_pair(uint32_t xo, uint32_t yo,
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Repacked layout 1: nibbles (t, t+4) of a word hold (k_2t, k_2t+1) + 8.
+__device__ __forceinline__ uint32_t expand_r16_pair(uint32_t v, int t, __half2 s2) {
+  uint32_t bits = ((v >> (4 * t)) & 0x000F000Fu) | 0x64006400u;
+  __half2 h = *reinterpret_cast<__half2*>(&bits);
+  h = __hsub2(h, __half2half2(__ushort_as_half((unsigned short)0x6408u)));
+  h = __hmul2(h, s2);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// acc(pair) += s * (bits_as_float(r pair) - 1.5 * 2^23), two lanes per op.
+__device__ __forceinline__ void acc2_magic(float& a0, float& a1, uint32_t r0, uint32_t r1, float s) {
+  asm("{\n\t.reg .b64 ac, rv, mg, sc;\n\t"
+      "mov.b64 ac, {%0, %1};\n\t"
+      "mov.b64 rv, {%2, %3};\n\t"
+      "mov.b64 mg, {%4, %4};\n\t"
+      "mov.b64 sc, {%5, %5};\n\t"
+      "add.rn.f32x2 rv, rv, mg;\n\t"
+      "fma.rn.f32x2 ac, rv, sc, ac;\n\t"
+      "mov.b64 {%0, %1}, ac;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "r"(r0), "r"(r1), "f"(-kMagicF), "f"(s));
+}
+
+// Store 32 consecutive tokens [m0, m0 + 32) of output feature n:
+// out[m, n] = v[j] * s_a[m] + bias_n - rowsum[m] * zpc_n.  Lane j loads the
+// per-token factors of token m0 + j (coalesced) and shuffles them to all.
+template <typename T>
+__device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const float* v, int m0, int n,
+                                              bool nvalid, float bias_n, float zpc_n, int lane) {
+  const int ml = m0 + lane;
+  const float sa_l = (ml < a.M) ? __ldg(&a.s_a[ml]) : 0.f;
+  const float rs_l = (a.rowsum && ml < a.M) ? __ldg(&a.rowsum[ml]) : 0.f;
+  const int jmax = nvalid ? min(32, a.M - m0) : 0;   // valid tokens in this chunk
+  T* p = out + (size_t)m0 * a.ldo + n;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float sa = __shfl_sync(0xffffffffu, sa_l, j);
+    const float rs = __shfl_sync(0xffffffffu, rs_l, j);
+    const float y = fmaf(-rs, zpc_n, fmaf(v[j], sa, bias_n));
+    if (j < jmax) {
+      if constexpr (sizeof(T) == 4) *p = y;
+      else if constexpr (std::is_same<T, __half>::value) *p = __float2half_rn(y);
+      else *p = __float2bfloat16_rn(y);
+    }
+    p += a.ldo;
+  }
+}
+
+__device__ __forceinline__ void store_chunk(const GemmArgs& a, const float* v, int m0, int n, bool nvalid,
+                                            float bias_n, float zpc_n, int lane) {
+  if (a.out_dtype == IC_DTYPE_F16)
+    store_chunk_t(a, reinterpret_cast<__half*>(a.out), v, m0, n, nvalid, bias_n, zpc_n, lane);
+  else if (a.out_dtype == IC_DTYPE_BF16)
+    store_chunk_t(a, reinterpret_cast<__nv_bfloat16*>(a.out), v, m0, n, nvalid, bias_n, zpc_n, lane);
+  else
+    store_chunk_t(a, reinterpret_cast<float*>(a.out), v, m0, n, nvalid, bias_n, zpc_n, lane);
+}
+
+// W4A16: out[m, n] = fp16(v[j] + bias_n) (no activation scale).
+__device__ __forceinline__ void store_chunk_raw(const GemmArgs& a, const float* v, int m0, int n, bool nvalid,
+                                                float bias_n) {
+  __half* out = reinterpret_cast<__half*>(a.out);
+  const int jmax = nvalid ? min(32, a.M - m0) : 0;
+  __half* p = out + (size_t)m0 * a.ldo + n;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < jmax) *p = __float2half_rn(v[j] + bias_n);
+    p += a.ldo;
+  }
+}
+
 }  // namespace ic
 
 namespace ic {
@@ -118,28 +208,34 @@ __global__ void __launch_bounds__(Cfg<MODE, BN, GROUPED>::THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                const GemmArgs a) {
   using C = Cfg<MODE, BN, GROUPED>;
-  constexpr int S = C::STAGES;
+  constexpr int SX = C::S_X, SW = C::S_W, SP = C::S_P;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C::STAGE_BYTES);
-  uint64_t* full = bars;            // TMA -> consumers         (count 1 + tx)
-  uint64_t* wready = bars + S;      // expansion warps -> MMA   (count 2)
-  uint64_t* empty = bars + 2 * S;   // MMA commit -> TMA        (count 1)
-  uint64_t* acc_full = bars + 3 * S;        // [2] MMA commit -> epilogue
-  uint64_t* acc_empty = bars + 3 * S + 2;   // [2] epilogue -> MMA (count EPI)
-  uint64_t* drain = bars + 3 * S + 4;       // abort path: MMA completion
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 5);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * S + 6);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* x_full = bars;                    // [SX] TMA -> MMA (count 1 + tx)
+  uint64_t* x_empty = bars + SX;              // [SX] MMA commit -> TMA
+  uint64_t* w_full = bars + 2 * SX;           // [SW] expansion -> MMA (I4)
+  uint64_t* w_empty = w_full + SW;            // [SW] MMA commit -> expansion (I4)
+  uint64_t* p_full = w_empty + SW;            // [SP] TMA -> expansion (I4)
+  uint64_t* acc_full = p_full + SP;           // [2] MMA commit -> epilogue
+  uint64_t* acc_empty = acc_full + 2;         // [2] epilogue -> MMA (count EPI)
+  uint64_t* drain = acc_empty + 2;            // abort path: MMA completion
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&wready[s], 2);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < SX; ++s) {
+      mbar_init(&x_full[s], 1);
+      mbar_init(&x_empty[s], 1);
     }
+    for (int s = 0; s < SW; ++s) {
+      mbar_init(&w_full[s], 1);
+      mbar_init(&w_empty[s], 1);
+    }
+    for (int s = 0; s < SP; ++s) mbar_init(&p_full[s], 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], C::EPI);
@@ -164,34 +260,32 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   const int total_tiles = a.m_tiles * a.n_tiles;
   const int units = GROUPED ? a.G : 1;
 
-  auto stage_w = [&](int s) { return smem + s * C::STAGE_BYTES; };
-  auto stage_x = [&](int s) { return smem + s * C::STAGE_BYTES + C::W_BYTES; };
-  auto stage_p = [&](int s) { return smem + s * C::STAGE_BYTES + C::W_BYTES + C::X_BYTES; };
+  auto x_stage = [&](int s) { return smem + s * C::XSTAGE + (C::I4 ? 0 : C::W_BYTES); };
+  auto w_stage = [&](int s) {
+    return C::I4 ? smem + C::OFF_W + s * C::W_BYTES : smem + s * C::XSTAGE;
+  };
+  auto p_stage = [&](int s) { return smem + C::OFF_P + s * C::P_BYTES; };
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------- TMA producer (X, and W for W_I8)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
         const int n_blk = tile / a.m_tiles, m_blk = tile % a.m_tiles;
         for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
-          const int s = it % S;
-          const uint32_t ph = (uint32_t)(it / S) & 1u;
-          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
-          constexpr uint32_t wbytes = (MODE == W_I8) ? C::W_BYTES : C::P_BYTES;
-          mbar_arrive_expect_tx(&full[s], (uint32_t)C::X_BYTES + wbytes);
-          tma_load_2d(stage_x(s), &tm_x, &full[s], kb * C::KB_ELEMS, m_blk * BN);
-          if constexpr (MODE == W_I8) tma_load_2d(stage_w(s), &tm_w, &full[s], kb * 128, n_blk * kTileN);
-          else if constexpr (MODE == W_I4) tma_load_2d(stage_p(s), &tm_w, &full[s], kb * 64, n_blk * kTileN);
-          else tma_load_2d(stage_p(s), &tm_w, &full[s], kb * 32, n_blk * kTileN);
+          const int s = it % SX;
+          const uint32_t ph = (uint32_t)(it / SX) & 1u;
+          if (!mbar_wait(&x_empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&x_full[s], (uint32_t)C::XSTAGE);
+          tma_load_2d(x_stage(s), &tm_x, &x_full[s], kb * C::KB_ELEMS, m_blk * BN);
+          if constexpr (MODE == W_I8) tma_load_2d(w_stage(s), &tm_w, &x_full[s], kb * 128, n_blk * kTileN);
         }
       }
       if (!ok) {
-        // let the copies already issued land before the CTA exits
         volatile int never = 0;
-        const int first = it > S ? it - S : 0;
-        for (int j = first; j < it; ++j) mbar_wait(&full[j % S], (uint32_t)(j / S) & 1u, &never);
+        const int first = it > SX ? it - SX : 0;
+        for (int j = first; j < it; ++j) mbar_wait(&x_full[j % SX], (uint32_t)(j / SX) & 1u, &never);
       }
     }
   } else if (warp == 1) {
@@ -209,22 +303,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           tc_fence_after();
           const uint32_t d = tmem_base + (uint32_t)(b * BN);
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
-            const int s = it % S;
-            const uint32_t ph = (uint32_t)(it / S) & 1u;
-            if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
-            if constexpr (MODE != W_I8) {
-              if (!mbar_wait(&wready[s], ph, abort_flag)) { ok = false; break; }
+            const int sx = it % SX;
+            if (!mbar_wait(&x_full[sx], (uint32_t)(it / SX) & 1u, abort_flag)) { ok = false; break; }
+            const int sw = C::I4 ? it % SW : sx;
+            if constexpr (C::I4) {
+              if (!mbar_wait(&w_full[sw], (uint32_t)(it / SW) & 1u, abort_flag)) { ok = false; break; }
             }
             tc_fence_after();
-            const uint64_t adesc = smem_desc_sw128(smem_u32(stage_w(s)));
-            const uint64_t bdesc = smem_desc_sw128(smem_u32(stage_x(s)));
+            const uint64_t adesc = smem_desc_sw128(smem_u32(w_stage(sw)));
+            const uint64_t bdesc = smem_desc_sw128(smem_u32(x_stage(sx)));
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const uint32_t acc = GROUPED ? 1u : ((kb > kb0 || k > 0) ? 1u : 0u);
               if constexpr (MODE == W_I4F) mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, acc);
               else mma_i8(d, adesc + 2 * k, bdesc + 2 * k, idesc, acc);
             }
-            mma_commit(&empty[s]);
+            mma_commit(&x_empty[sx]);
+            if constexpr (C::I4) mma_commit(&w_empty[sw]);
           }
           if (!ok) break;
           mma_commit(&acc_full[b]);
@@ -237,37 +332,64 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       }
     }
   } else if (warp < 4) {
-    // ------------------------------------------------------------ INT4 expansion
-    if constexpr (MODE != W_I8) {
-      const int u = threadIdx.x - 64;   // 0..63
+    // ------------------------------------- INT4 expansion (+ packed-tile TMA)
+    // Warp 2 handles the even K blocks of the CTA's sequence, warp 3 the odd
+    // ones; each waits for its own packed stage, expands it into a weight
+    // stage, and re-arms the packed stage with the block SP steps ahead.
+    if constexpr (C::I4) {
+      const int xw = warp - 2;
+      int issued = 0;
+      auto issue_p = [&](int j) {
+        const int tile_j = blockIdx.x + (j / a.num_kb) * gridDim.x;
+        if (tile_j >= total_tiles) return;
+        const int kb = j % a.num_kb;
+        const int n_blk = tile_j / a.m_tiles;
+        const int sp = j % SP;
+        mbar_arrive_expect_tx(&p_full[sp], (uint32_t)C::P_BYTES);
+        tma_load_2d(p_stage(sp), &tm_w, &p_full[sp], kb * (MODE == W_I4 ? 64 : 32), n_blk * kTileN);
+        issued = j + 1;
+      };
+      if (lane == 0)
+        for (int j = xw; j < SP; j += 2) issue_p(j);
       int it = 0;
       bool ok = true;
+      const bool rp = a.w_repacked != 0;
       for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
         const int n_blk = tile / a.m_tiles;
         for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
-          const int s = it % S;
-          const uint32_t ph = (uint32_t)(it / S) & 1u;
-          if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
-          uint8_t* W = stage_w(s);
-          const uint8_t* P = stage_p(s);
+          if ((it & 1) != xw) continue;
+          const int sp = it % SP, sw = it % SW;
+          bool w_ok = mbar_wait(&p_full[sp], (uint32_t)(it / SP) & 1u, abort_flag);
+          if (w_ok) w_ok = mbar_wait(&w_empty[sw], ((uint32_t)(it / SW) & 1u) ^ 1u, abort_flag);
+          if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
+          uint8_t* W = w_stage(sw);
+          const uint8_t* P = p_stage(sp);
           if constexpr (MODE == W_I4) {
-#pragma unroll 2
-            for (int i = 0; i < 8; ++i) {
-              const int r = i * 16 + (u >> 2), c = u & 3;
+#pragma unroll 4
+            for (int i = 0; i < 16; ++i) {
+              const int r = i * 8 + (lane >> 2), c = lane & 3;
               const uint4 p = *reinterpret_cast<const uint4*>(P + r * 64 + c * 16);
               uint4 o0, o1;
-              expand_i4_i8(p.x, o0.x, o0.y);
-              expand_i4_i8(p.y, o0.z, o0.w);
-              expand_i4_i8(p.z, o1.x, o1.y);
-              expand_i4_i8(p.w, o1.z, o1.w);
+              if (rp) {
+                // layout 0: byte b of a word = q[k_b] | q[k_{b+4}] << 4
+                o0.x = (p.x << 4) & 0xF0F0F0F0u; o0.y = p.x & 0xF0F0F0F0u;
+                o0.z = (p.y << 4) & 0xF0F0F0F0u; o0.w = p.y & 0xF0F0F0F0u;
+                o1.x = (p.z << 4) & 0xF0F0F0F0u; o1.y = p.z & 0xF0F0F0F0u;
+                o1.z = (p.w << 4) & 0xF0F0F0F0u; o1.w = p.w & 0xF0F0F0F0u;
+              } else {
+                expand_i4_i8(p.x, o0.x, o0.y);
+                expand_i4_i8(p.y, o0.z, o0.w);
+                expand_i4_i8(p.z, o1.x, o1.y);
+                expand_i4_i8(p.w, o1.z, o1.w);
+              }
               *reinterpret_cast<uint4*>(W + sw128_offset(r, 2 * c)) = o0;
               *reinterpret_cast<uint4*>(W + sw128_offset(r, 2 * c + 1)) = o1;
             }
           } else {
             const int g = (a.G > 1) ? (kb * 64) / a.group_size : 0;
 #pragma unroll 2
-            for (int i = 0; i < 4; ++i) {
-              const int r = i * 32 + (u >> 1), c = u & 1;
+            for (int i = 0; i < 8; ++i) {
+              const int r = i * 16 + (lane >> 1), c = lane & 1;
               const int n = n_blk * kTileN + r;
               __half sh = __float2half_rn(0.f);
               if (n < a.N) {
@@ -281,21 +403,36 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
               const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
 #pragma unroll
               for (int w = 0; w < 4; ++w) {
-                const uint32_t ob = pw[w] ^ 0x88888888u;
-                const uint32_t xo = ob & 0x0F0F0F0Fu, yo = (ob >> 4) & 0x0F0F0F0Fu;
                 uint4 o;
-                o.x = expand_i4_f16_pair(xo, yo, 0, s2);
-                o.y = expand_i4_f16_pair(xo, yo, 1, s2);
-                o.z = expand_i4_f16_pair(xo, yo, 2, s2);
-                o.w = expand_i4_f16_pair(xo, yo, 3, s2);
+                if (rp) {
+                  o.x = expand_r16_pair(pw[w], 0, s2);
+                  o.y = expand_r16_pair(pw[w], 1, s2);
+                  o.z = expand_r16_pair(pw[w], 2, s2);
+                  o.w = expand_r16_pair(pw[w], 3, s2);
+                } else {
+                  const uint32_t ob = pw[w] ^ 0x88888888u;
+                  const uint32_t xo = ob & 0x0F0F0F0Fu, yo = (ob >> 4) & 0x0F0F0F0Fu;
+                  o.x = expand_i4_f16_pair(xo, yo, 0, s2);
+                  o.y = expand_i4_f16_pair(xo, yo, 1, s2);
+                  o.z = expand_i4_f16_pair(xo, yo, 2, s2);
+                  o.w = expand_i4_f16_pair(xo, yo, 3, s2);
+                }
                 *reinterpret_cast<uint4*>(W + sw128_offset(r, 4 * c + w)) = o;
               }
             }
           }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&wready[s]);
+          if (lane == 0) {
+            mbar_arrive(&w_full[sw]);
+            issue_p(it + SP);   // same parity as it: this warp's next use of the stage
+          }
         }
+      }
+      if (!ok && lane == 0) {
+        volatile int never = 0;
+        for (int j = it; j < issued; ++j)
+          if ((j & 1) == xw) mbar_wait(&p_full[j % SP], (uint32_t)(j / SP) & 1u, &never);
       }
     }
   } else {
@@ -309,8 +446,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
 #pragma unroll
       for (int b = 0; b < 2; ++b)
 #pragma unroll
-        for (int c = 0; c < C::CPT / 32; ++c)
-          tmem_st32_const(tmem_base + lane_base + (uint32_t)(b * BN + col0 + 32 * c), kMagic);
+        for (int c = 0; c < C::CPT / 16; ++c)
+          tmem_st16_const(tmem_base + lane_base + (uint32_t)(b * BN + col0 + 16 * c), kMagic);
       tmem_wait_st();
     }
     tc_fence_before();
@@ -332,39 +469,35 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         float acc[C::CPT];
 #pragma unroll
         for (int j = 0; j < C::CPT; ++j) acc[j] = 0.f;
+        const float* swrow = a.s_w + (size_t)(nvalid ? n : 0) * a.G;
+        float sw = nvalid ? __ldg(swrow) * wmul : 0.f;
         for (int u = 0; u < units; ++u, ++uc) {
           const int b = uc & 1;
-          const float sw = nvalid ? __ldg(&a.s_w[(size_t)n * a.G + u]) * wmul : 0.f;
+          // next group's scale is fetched while this group is consumed
+          const float sw_next = (nvalid && u + 1 < units) ? __ldg(swrow + u + 1) * wmul : 0.f;
           if (!mbar_wait(&acc_full[b], (uint32_t)(uc >> 1) & 1u, abort_flag)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < C::CPT / 32; ++c) {
-            const uint32_t ta = tmem_base + lane_base + (uint32_t)(b * BN + col0 + 32 * c);
-            uint32_t r[32];
-            tmem_ld32(ta, r);
+          for (int c = 0; c < C::CPT / 16; ++c) {
+            const uint32_t ta = tmem_base + lane_base + (uint32_t)(b * BN + col0 + 16 * c);
+            uint32_t r[16];
+            tmem_ld16(ta, r);
             tmem_wait_ld();
-            tmem_st32_const(ta, kMagic);
+            tmem_st16_const(ta, kMagic);
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              acc[32 * c + j] = fmaf(__uint_as_float(r[j]) - kMagicF, sw, acc[32 * c + j]);
+            for (int j = 0; j < 8; ++j)
+              acc2_magic(acc[16 * c + 2 * j], acc[16 * c + 2 * j + 1], r[2 * j], r[2 * j + 1], sw);
           }
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[b]);
+          sw = sw_next;
         }
         if (!ok) break;
-        if (nvalid) {
 #pragma unroll
-          for (int j = 0; j < C::CPT; ++j) {
-            const int m = mbase + j;
-            if (m < a.M) {
-              float v = fmaf(acc[j], __ldg(&a.s_a[m]), bias_n);
-              if (a.rowsum) v = fmaf(-__ldg(&a.rowsum[m]), zpc_n, v);
-              store_out(a.out, a.out_dtype, (size_t)m * a.ldo + n, v);
-            }
-          }
-        }
+        for (int c = 0; c < C::CPT / 32; ++c)
+          store_chunk(a, acc + 32 * c, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane);
       } else {
         const int b = uc & 1;
         const float sw = (MODE == W_I4F) ? 1.f : (nvalid ? __ldg(&a.s_w[n]) * wmul : 0.f);
@@ -376,22 +509,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           uint32_t r[32];
           tmem_ld32(ta, r);
           tmem_wait_ld();
-          if (nvalid) {
+          float v[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int m = mbase + 32 * c + j;
-              if (m < a.M) {
-                float v;
-                if constexpr (MODE == W_I4F) {
-                  v = __uint_as_float(r[j]) + bias_n;
-                } else {
-                  v = fmaf((float)(int)r[j] * sw, __ldg(&a.s_a[m]), bias_n);
-                  if (a.rowsum) v = fmaf(-__ldg(&a.rowsum[m]), zpc_n, v);
-                }
-                store_out(a.out, a.out_dtype, (size_t)m * a.ldo + n, v);
-              }
-            }
-          }
+          for (int j = 0; j < 32; ++j)
+            v[j] = (MODE == W_I4F) ? __uint_as_float(r[j]) : (float)(int)r[j] * sw;
+          if constexpr (MODE == W_I4F) store_chunk_raw(a, v, mbase + 32 * c, n, nvalid, bias_n);
+          else store_chunk(a, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane);
         }
         tc_fence_before();
         __syncwarp();
@@ -409,7 +532,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
 }
 
 }  // namespace ic
-
 // ============================================================== host side
 namespace ic {
 
@@ -469,12 +591,24 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tw, const CUtensorMap& tx, c
   return cudaGetLastError();
 }
 
-// Token-tile width for M tokens.
+// Token-tile width for M tokens.  INTCRUSH_FORCE_BN (32/64/128/192/256)
+// overrides the choice; it exists for tuning runs.
+static int forced_bn() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("INTCRUSH_FORCE_BN");
+    v = e ? atoi(e) : 0;
+  }
+  return v;
+}
+
 static int pick_bn(int M, bool grouped) {
+  const int f = forced_bn();
+  if (f) return f;
   if (M <= 32) return 32;
   if (M <= 64) return 64;
   if (M <= 128) return 128;
-  return grouped ? 192 : 256;
+  return 256;
 }
 
 template <int MODE, bool GROUPED>
@@ -488,9 +622,7 @@ static cudaError_t dispatch_bn(int bn, const CUtensorMap& tw, const CUtensorMap&
     case 192:
       if constexpr (GROUPED) return launch_gemm_t<MODE, 192, GROUPED>(tw, tx, a, st);
       else return cudaErrorInvalidValue;
-    case 256:
-      if constexpr (!GROUPED) return launch_gemm_t<MODE, 256, GROUPED>(tw, tx, a, st);
-      else return cudaErrorInvalidValue;
+    case 256: return launch_gemm_t<MODE, 256, GROUPED>(tw, tx, a, st);
     default: return cudaErrorInvalidValue;
   }
 }

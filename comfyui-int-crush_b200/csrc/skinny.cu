@@ -29,6 +29,15 @@ __device__ __forceinline__ uint32_t i4pair_f16(uint32_t xo, uint32_t yo, int i, 
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Layout 1 of ic_repack_int4: nibbles (t, t+4) of a word hold (k_2t, k_2t+1) + 8.
+__device__ __forceinline__ uint32_t r16pair_f16(uint32_t v, int t, __half2 s2) {
+  uint32_t bits = ((v >> (4 * t)) & 0x000F000Fu) | 0x64006400u;
+  __half2 h = *reinterpret_cast<__half2*>(&bits);
+  h = __hsub2(h, __half2half2(__ushort_as_half((unsigned short)0x6408u)));
+  h = __hmul2(h, s2);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -45,6 +54,7 @@ struct SkinnyArgs {
   const void* bias; int bias_dtype;
   const __half* lr_mid; const __half* lr_up; int R; float lr_scale;
   __half* out; long long ldo;
+  int repacked;     // weights in ic_repack_int4 layout 1
 };
 
 __device__ __forceinline__ uint4 load_packed16(const SkinnyArgs& a, int n, int kb, int t) {
@@ -115,12 +125,20 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps) w4a16_skinny_kernel(const S
       const uint32_t xa = oa & 0x0F0F0F0Fu, ya = (oa >> 4) & 0x0F0F0F0Fu;
       const uint32_t xb = ob & 0x0F0F0F0Fu, yb = (ob >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {   // MMA step s = 2w + h uses bytes 2h, 2h+1 of word w
+      for (int h = 0; h < 2; ++h) {   // MMA step s = 2w + h uses k pairs 2h, 2h+1 of word w
         const int s = 2 * w + h;
-        const uint32_t a0 = i4pair_f16(xa, ya, 2 * h, sa);
-        const uint32_t a2 = i4pair_f16(xa, ya, 2 * h + 1, sa);
-        const uint32_t a1 = i4pair_f16(xb, yb, 2 * h, sb);
-        const uint32_t a3 = i4pair_f16(xb, yb, 2 * h + 1, sb);
+        uint32_t a0, a1, a2, a3;
+        if (a.repacked) {
+          a0 = r16pair_f16(wa[w], 2 * h, sa);
+          a2 = r16pair_f16(wa[w], 2 * h + 1, sa);
+          a1 = r16pair_f16(wb[w], 2 * h, sb);
+          a3 = r16pair_f16(wb[w], 2 * h + 1, sb);
+        } else {
+          a0 = i4pair_f16(xa, ya, 2 * h, sa);
+          a2 = i4pair_f16(xa, ya, 2 * h + 1, sa);
+          a1 = i4pair_f16(xb, yb, 2 * h, sb);
+          a3 = i4pair_f16(xb, yb, 2 * h + 1, sb);
+        }
 #pragma unroll
         for (int i = 0; i < TT; ++i) mma_16816(d[i], a0, a1, a2, a3, xw[i][2 * s], xw[i][2 * s + 1]);
       }
@@ -249,6 +267,52 @@ __global__ void unpack_i4_f16_kernel(const uint8_t* p, int N, int K, long long l
   const __half s = scale_dtype == IC_DTYPE_F16 ? reinterpret_cast<const __half*>(scale)[si]
                                                : __float2half_rn(reinterpret_cast<const float*>(scale)[si]);
   out[i] = __hmul(__int2half_rn(v), s);
+}
+
+// ------------------------------------------------------------ repack
+// Reference packing: byte j of a row = q[2j] | q[2j+1] << 4 (low nibble = even
+// k, _quant_utils.py:170-182).  Repacked layouts keep the row size and permute
+// nibbles inside each 4-byte word (8 consecutive k) so that the GEMM's INT4
+// expansion needs only shifts and masks:
+//   layout 0 (W4A8):  byte b = q[b] | q[b+4] << 4                (two's complement)
+//   layout 1 (W4A16): nibble t = q[2t] + 8, nibble t+4 = q[2t+1] + 8 (offset binary)
+__global__ void repack_i4_kernel(const uint8_t* src, int N, int K, long long lds, uint8_t* dst, long long ldd,
+                                 int layout) {
+  const long long words = (K + 7) / 8;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)N * words) return;
+  const long long n = i / words, w = i % words;
+  const int nbytes = (K + 1) / 2;
+  uint32_t q[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const long long k = w * 8 + t;
+    uint32_t v = 0;
+    if (k < K) {
+      const uint8_t b = src[n * lds + k / 2];
+      v = (k & 1) ? (b >> 4) : (b & 15);
+    }
+    q[t] = v;
+  }
+  uint32_t out = 0;
+  if (layout == 0) {
+#pragma unroll
+    for (int b = 0; b < 4; ++b) out |= (q[b] | (q[b + 4] << 4)) << (8 * b);
+  } else {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) out |= ((q[2 * t] ^ 8u) << (4 * t)) | ((q[2 * t + 1] ^ 8u) << (4 * (t + 4)));
+  }
+#pragma unroll
+  for (int b = 0; b < 4; ++b)
+    if (w * 4 + b < nbytes) dst[n * ldd + w * 4 + b] = (uint8_t)(out >> (8 * b));
+}
+
+cudaError_t launch_repack(const uint8_t* src, int N, int K, long long lds, uint8_t* dst, long long ldd, int layout,
+                          cudaStream_t st) {
+  const long long total = (long long)N * ((K + 7) / 8);
+  if (total == 0) return cudaSuccess;
+  repack_i4_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, N, K, lds, dst, ldd, layout);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_unpack_i8(const uint8_t* p, int N, int K, long long ldp, int8_t* out, cudaStream_t st) {

@@ -39,6 +39,7 @@ extern "C" {
 #define IC_W_INT8 0           /* int8  [N, K], row stride ldw bytes         */
 #define IC_W_INT4 1           /* uint8 [N, K/2] two signed nibbles per byte,
                                  low nibble = even k (two's complement)     */
+#define IC_W_INT4R 2          /* same shape, ic_repack_int4 layout 0        */
 
 /* Library version, (major << 16) | minor. */
 int ic_version(void);
@@ -97,6 +98,7 @@ int ic_dynamic_quantize(const void* x, int x_dtype, int64_t M, int64_t K, int64_
  *   xq      [M, K] int8, row stride ldq bytes (ldq % 16 == 0)
  *   w       IC_W_INT8: int8 [N, K] (ldw % 16 == 0, K % 16 == 0)
  *           IC_W_INT4: uint8 [N, ceil(K/2)] (ldw % 16 == 0, K % 32 == 0)
+ *           IC_W_INT4R: as IC_W_INT4 in ic_repack_int4 layout 0 (faster)
  *   s_w     fp32 [N, G] row-major; G == 1 is per-channel, G > 1 groups of
  *           group_size consecutive k (group_size % 128 == 0); the group form
  *           follows _quant_utils.py:255-270
@@ -123,7 +125,8 @@ int ic_gemm_a8(const int8_t* xq, int64_t M, int64_t K, int64_t ldq,
  * LoRA residual (_ops.py:236-244) for standard LoRA.
  *
  *   x      [M, K] fp16 (x_dtype must be IC_DTYPE_F16), row stride ldx
- *   w      uint8 [N, ceil(K/2)], row stride ldw bytes
+ *   w      uint8 [N, ceil(K/2)], row stride ldw bytes; w_layout 0 = the
+ *          reference packing, 1 = ic_repack_int4 layout 1 (faster)
  *   scale  [N, G] in scale_dtype (f16 or f32; cast to fp16 like the
  *          reference), group_size % 128 == 0 when G > 1
  *   bias   [N] or NULL
@@ -131,7 +134,7 @@ int ic_gemm_a8(const int8_t* xq, int64_t M, int64_t K, int64_t ldq,
  *   out    [M, N] fp16, row stride ldo
  */
 int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
-                  const uint8_t* w, int64_t N, int64_t ldw,
+                  const uint8_t* w, int64_t N, int64_t ldw, int w_layout,
                   const void* scale, int scale_dtype, int64_t G, int64_t group_size,
                   const void* bias, int bias_dtype,
                   const void* lr_mid, const void* lr_up, int64_t R, float lr_scale,
@@ -147,6 +150,16 @@ int ic_lowrank_down(const void* x, int64_t M, int64_t K, int64_t ldx, const void
  * mid [M, R] fp16, up [N, R] fp16. */
 int ic_lowrank_add(void* out, int64_t M, int64_t N, int64_t ldo, const void* mid,
                    const void* up, int64_t R, float scale, void* stream);
+
+/* Load-time weight repack.  The reference's packing (_quant_utils.py:
+ * 170-182) stays the input format; this permutes the nibbles of each 4-byte
+ * word (8 consecutive k) so the GEMMs expand INT4 with shifts and masks only.
+ * layout 0 (for ic_gemm_a8, IC_W_INT4R): byte b of a word = q[b] | q[b+4] << 4;
+ * layout 1 (for ic_gemm_w4a16, w_layout 1): nibble t = q[2t] + 8, nibble t+4 =
+ * q[2t+1] + 8.  src/dst [N, ceil(K/2)] uint8 with row strides lds/ldd; src and
+ * dst must not overlap. */
+int ic_repack_int4(const uint8_t* src, int64_t N, int64_t K, int64_t lds, uint8_t* dst, int64_t ldd,
+                   int layout, void* stream);
 
 /* unpack_int4_to_int8 (kernels/triton_int4_to_int8_unpack.py:55-81):
  * packed [N, ldp bytes] -> out int8 [N, K] (row stride K). */

@@ -176,6 +176,60 @@ def test_gemm_a8_zero_point_term():
     assert O.max_rel(out.cpu().numpy(), ref) <= 1e-5
 
 
+@pytest.mark.parametrize("G", [1, 24])
+@pytest.mark.parametrize("M", [1, 64, 300])
+def test_gemm_a8_repacked_int4_bit_identical(G, M):
+    """The load-time repacked layout gives the same output bits as the reference packing."""
+    dev = _dev()
+    N, K = 256, 3072
+    xq, wq = _int_inputs(M, N, K, seed=M + G, int4=True)
+    rng = np.random.default_rng(7)
+    s_w = rng.uniform(1e-3, 2e-2, (N, G)).astype(np.float32)
+    s_a = rng.uniform(1e-3, 5e-2, M).astype(np.float32)
+    packed = _t(O.pack_int4(wq), dev)
+    rep = rt.repack_int4(packed, K, 0)
+    a = rt.gemm_a8(_t(xq, dev), packed, _t(s_w, dev), _t(s_a, dev), out_dtype=torch.float32, group_size=K // G)
+    b = rt.gemm_a8(_t(xq, dev), rep, _t(s_w, dev), _t(s_a, dev), out_dtype=torch.float32, group_size=K // G,
+                   repacked=True)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("M", [1, 16, 33, 256])
+def test_w4a16_repacked_bit_identical(M):
+    dev = _dev()
+    N, K = 512, 3072
+    rng = np.random.default_rng(M)
+    x = _t(rng.standard_normal((M, K)).astype(np.float16), dev)
+    packed = _t(O.pack_int4(rng.integers(-8, 8, (N, K)).astype(np.int8)), dev)
+    scale = _t(rng.uniform(1e-3, 2e-2, (N, 24)).astype(np.float16), dev)
+    a = rt.gemm_w4a16(x, packed, scale, group_size=128)
+    b = rt.gemm_w4a16(x, rt.repack_int4(packed, K, 1), scale, group_size=128, w_layout=1)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("bn", [32, 64, 128, 192, 256])
+def test_gemm_a8_grouped_every_tile_width(bn, monkeypatch):
+    """Each token-tile width of the group-scale kernel, in a fresh process."""
+    import subprocess, sys, os
+    dev = _dev()
+    code = (
+        "import sys; sys.path[:0] = %r\n"
+        "import conftest, numpy as np, torch, intcrush_oracle as O\n"
+        "from _pkg import load\n"
+        "rt = load('_b200_runtime')\n"
+        "rng = np.random.default_rng(5); M, N, K = 300, 256, 1024\n"
+        "xq = rng.integers(-128, 128, (M, K)).astype(np.int8); wq = rng.integers(-8, 8, (N, K)).astype(np.int8)\n"
+        "s_w = rng.uniform(1e-3, 2e-2, (N, 8)).astype(np.float32); s_a = rng.uniform(1e-3, 5e-2, M).astype(np.float32)\n"
+        "t = lambda a: torch.from_numpy(a).cuda()\n"
+        "out = rt.gemm_a8(t(xq), rt.repack_int4(t(O.pack_int4(wq)), K, 0), t(s_w), t(s_a), out_dtype=torch.float32, group_size=128, repacked=True)\n"
+        "err = O.max_rel(out.cpu().numpy(), O.gemm_a8(xq, s_a, wq, s_w, group_size=128))\n"
+        "assert err <= 1e-5, err\n"
+    ) % ([os.path.dirname(__file__)],)
+    env = dict(os.environ, INTCRUSH_FORCE_BN=str(bn))
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+
+
 def test_gemm_a8_unpacked_int4_matches_packed():
     dev = _dev()
     M, N, K = 64, 256, 1024
