@@ -12,7 +12,7 @@ import os
 import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libintcrush_b200.so")
+LIB_PATH = os.environ.get("INTCRUSH_LIB") or os.path.join(_HERE, "libintcrush_b200.so")
 
 IC_OK = 0
 IC_ERR_ARG = 1

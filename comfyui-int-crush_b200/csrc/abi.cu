@@ -43,6 +43,14 @@ extern "C" {
 
 int ic_version(void) { return (1 << 16) | 0; }
 
+#if defined(IC_TRACE)
+int ic_trace_read(unsigned long long* out, int clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, ic::g_ic_trace, sizeof(unsigned long long) * 16);
+  if (clear) { unsigned long long z[16] = {0}; cudaMemcpyToSymbol(ic::g_ic_trace, z, sizeof(z)); }
+  return e == cudaSuccess ? 0 : 3;
+}
+#endif
+
 const char* ic_last_error(void) { return g_err; }
 
 int ic_read_device_error(int clear, int* code_out) {

@@ -137,6 +137,22 @@ __device__ __forceinline__ uint32_t expand_r16_pair(uint32_t v, int t, __half2 s
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Packed accumulator pair (two fp32 in one 64-bit register):
+// acc += s2 * (bits_as_float(r pair) + mg2), with mg2 = (-1.5 * 2^23) x 2.
+__device__ __forceinline__ void acc2p(unsigned long long& acc, uint32_t r0, uint32_t r1,
+                                      unsigned long long s2, unsigned long long mg2) {
+  asm("{\n\t.reg .b64 rv;\n\t"
+      "mov.b64 rv, {%1, %2};\n\t"
+      "add.rn.f32x2 rv, rv, %4;\n\t"
+      "fma.rn.f32x2 %0, rv, %3, %0;\n\t}"
+      : "+l"(acc)
+      : "r"(r0), "r"(r1), "l"(s2), "l"(mg2));
+}
+
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+  return ((unsigned long long)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+
 // acc(pair) += s * (bits_as_float(r pair) - 1.5 * 2^23), two lanes per op.
 __device__ __forceinline__ void acc2_magic(float& a0, float& a1, uint32_t r0, uint32_t r1, float s) {
   asm("{\n\t.reg .b64 ac, rv, mg, sc;\n\t"
@@ -162,10 +178,11 @@ __device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const f
   const float rs_l = (a.rowsum && ml < a.M) ? __ldg(&a.rowsum[ml]) : 0.f;
   const int jmax = nvalid ? min(32, a.M - m0) : 0;   // valid tokens in this chunk
   T* p = out + (size_t)m0 * a.ldo + n;
+  float sa_b = sa_l, rs_b = rs_l;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    const float sa = __shfl_sync(0xffffffffu, sa_l, j);
-    const float rs = __shfl_sync(0xffffffffu, rs_l, j);
+    const float sa = __shfl_sync(0xffffffffu, sa_b, j);
+    const float rs = __shfl_sync(0xffffffffu, rs_b, j);
     const float y = fmaf(-rs, zpc_n, fmaf(v[j], sa, bias_n));
     if (j < jmax) {
       if constexpr (sizeof(T) == 4) *p = y;
@@ -173,6 +190,9 @@ __device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const f
       else *p = __float2bfloat16_rn(y);
     }
     p += a.ldo;
+    // keep the compiler from hoisting all 32 shuffles (register pressure):
+    // the next 8 shuffles depend on this empty asm, issued after these stores
+    if ((j & 7) == 7) asm volatile("" : "+f"(sa_b), "+f"(rs_b)::"memory");
   }
 }
 
@@ -202,6 +222,17 @@ __device__ __forceinline__ void store_chunk_raw(const GemmArgs& a, const float* 
 }  // namespace ic
 
 namespace ic {
+
+#if defined(IC_TRACE)
+// Tuning-only instrumentation (never in the shipped build): cycles spent per
+// pipeline role, summed over CTAs.
+__device__ unsigned long long g_ic_trace[16];
+#define IC_T0() long long _t0 = clock64()
+#define IC_TADD(i) atomicAdd(&g_ic_trace[i], (unsigned long long)(clock64() - _t0))
+#else
+#define IC_T0()
+#define IC_TADD(i)
+#endif
 
 template <int MODE, int BN, bool GROUPED>
 __global__ void __launch_bounds__(Cfg<MODE, BN, GROUPED>::THREADS, 1)
@@ -276,7 +307,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
           const int s = it % SX;
           const uint32_t ph = (uint32_t)(it / SX) & 1u;
+          { IC_T0();
           if (!mbar_wait(&x_empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
+          IC_TADD(8); }
           mbar_arrive_expect_tx(&x_full[s], (uint32_t)C::XSTAGE);
           tma_load_2d(x_stage(s), &tm_x, &x_full[s], kb * C::KB_ELEMS, m_blk * BN);
           if constexpr (MODE == W_I8) tma_load_2d(w_stage(s), &tm_w, &x_full[s], kb * 128, n_blk * kTileN);
@@ -299,15 +332,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           const int kb0 = GROUPED ? u * a.kb_per_group : 0;
           const int kb1 = GROUPED ? min(kb0 + a.kb_per_group, a.num_kb) : a.num_kb;
           const int b = uc & 1;
+          { IC_T0();
           if (!mbar_wait(&acc_empty[b], (uint32_t)(uc >> 1) & 1u, abort_flag)) { ok = false; break; }
+          IC_TADD(0); }
           tc_fence_after();
           const uint32_t d = tmem_base + (uint32_t)(b * BN);
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int sx = it % SX;
+            { IC_T0();
             if (!mbar_wait(&x_full[sx], (uint32_t)(it / SX) & 1u, abort_flag)) { ok = false; break; }
+            IC_TADD(1); }
             const int sw = C::I4 ? it % SW : sx;
             if constexpr (C::I4) {
+              IC_T0();
               if (!mbar_wait(&w_full[sw], (uint32_t)(it / SW) & 1u, abort_flag)) { ok = false; break; }
+              IC_TADD(2);
             }
             tc_fence_after();
             const uint64_t adesc = smem_desc_sw128(smem_u32(w_stage(sw)));
@@ -359,8 +398,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
           if ((it & 1) != xw) continue;
           const int sp = it % SP, sw = it % SW;
+          IC_T0();
           bool w_ok = mbar_wait(&p_full[sp], (uint32_t)(it / SP) & 1u, abort_flag);
+          if (lane == 0) IC_TADD(5);
+#if defined(IC_TRACE)
+          _t0 = clock64();
+#endif
           if (w_ok) w_ok = mbar_wait(&w_empty[sw], ((uint32_t)(it / SW) & 1u) ^ 1u, abort_flag);
+          if (lane == 0) IC_TADD(6);
+#if defined(IC_TRACE)
+          _t0 = clock64();
+#endif
           if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
           uint8_t* W = w_stage(sw);
           const uint8_t* P = p_stage(sp);
@@ -423,6 +471,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           }
           fence_proxy_async_smem();
           __syncwarp();
+          if (lane == 0) IC_TADD(7);
           if (lane == 0) {
             mbar_arrive(&w_full[sw]);
             issue_p(it + SP);   // same parity as it: this warp's next use of the stage
@@ -466,17 +515,41 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       const float zpc_n = (nvalid && a.zp_corr) ? a.zp_corr[n] : 0.f;
       const int mbase = m_blk * BN + col0;
       if constexpr (GROUPED) {
-        float acc[C::CPT];
+        unsigned long long accp[C::CPT / 2];   // fp32 pairs
 #pragma unroll
-        for (int j = 0; j < C::CPT; ++j) acc[j] = 0.f;
+        for (int j = 0; j < C::CPT / 2; ++j) accp[j] = 0ull;
+        const unsigned long long mg2 = pack2(-kMagicF, -kMagicF);
         const float* swrow = a.s_w + (size_t)(nvalid ? n : 0) * a.G;
         float sw = nvalid ? __ldg(swrow) * wmul : 0.f;
         for (int u = 0; u < units; ++u, ++uc) {
           const int b = uc & 1;
           // next group's scale is fetched while this group is consumed
           const float sw_next = (nvalid && u + 1 < units) ? __ldg(swrow + u + 1) * wmul : 0.f;
+          IC_T0();
           if (!mbar_wait(&acc_full[b], (uint32_t)(uc >> 1) & 1u, abort_flag)) { ok = false; break; }
+          if (warp == 4 && lane == 0) IC_TADD(3);
+#if defined(IC_TRACE)
+          _t0 = clock64();
+          if (warp == 4 && lane == 0) atomicAdd(&g_ic_trace[10], 1ull);
+#endif
           tc_fence_after();
+          const unsigned long long sw2 = pack2(sw, sw);
+#if defined(IC_EPI_SINGLE_WAIT)
+          {
+            uint32_t r[C::CPT / 16][16];
+#pragma unroll
+            for (int c = 0; c < C::CPT / 16; ++c)
+              tmem_ld16(tmem_base + lane_base + (uint32_t)(b * BN + col0 + 16 * c), r[c]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < C::CPT / 16; ++c)
+              tmem_st16_const(tmem_base + lane_base + (uint32_t)(b * BN + col0 + 16 * c), kMagic);
+#pragma unroll
+            for (int c = 0; c < C::CPT / 16; ++c)
+#pragma unroll
+              for (int j = 0; j < 8; ++j) acc2p(accp[8 * c + j], r[c][2 * j], r[c][2 * j + 1], sw2, mg2);
+          }
+#else
 #pragma unroll
           for (int c = 0; c < C::CPT / 16; ++c) {
             const uint32_t ta = tmem_base + lane_base + (uint32_t)(b * BN + col0 + 16 * c);
@@ -485,19 +558,36 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
             tmem_wait_ld();
             tmem_st16_const(ta, kMagic);
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              acc2_magic(acc[16 * c + 2 * j], acc[16 * c + 2 * j + 1], r[2 * j], r[2 * j + 1], sw);
+            for (int j = 0; j < 8; ++j) {
+#if defined(IC_EPI_SCALAR)
+              float lo = __uint_as_float((uint32_t)accp[8 * c + j]), hi = __uint_as_float((uint32_t)(accp[8 * c + j] >> 32));
+              lo = fmaf(__uint_as_float(r[2 * j]) - kMagicF, sw, lo);
+              hi = fmaf(__uint_as_float(r[2 * j + 1]) - kMagicF, sw, hi);
+              accp[8 * c + j] = pack2(lo, hi);
+#else
+              acc2p(accp[8 * c + j], r[2 * j], r[2 * j + 1], sw2, mg2);
+#endif
+            }
           }
+#endif
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[b]);
+          if (warp == 4 && lane == 0) IC_TADD(4);
           sw = sw_next;
         }
         if (!ok) break;
 #pragma unroll
-        for (int c = 0; c < C::CPT / 32; ++c)
-          store_chunk(a, acc + 32 * c, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane);
+        for (int c = 0; c < C::CPT / 32; ++c) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            v[2 * j] = __uint_as_float((uint32_t)accp[16 * c + j]);
+            v[2 * j + 1] = __uint_as_float((uint32_t)(accp[16 * c + j] >> 32));
+          }
+          store_chunk(a, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane);
+        }
       } else {
         const int b = uc & 1;
         const float sw = (MODE == W_I4F) ? 1.f : (nvalid ? __ldg(&a.s_w[n]) * wmul : 0.f);
@@ -524,6 +614,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     }
   }
 
+#if defined(IC_TRACE)
+  if (threadIdx.x == 0) { IC_T0(); (void)_t0; }
+#endif
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
