@@ -701,7 +701,7 @@ static int pick_bn(int M, bool grouped) {
   if (M <= 32) return 32;
   if (M <= 64) return 64;
   if (M <= 128) return 128;
-  return 256;
+  return grouped ? 192 : 256;
 }
 
 template <int MODE, bool GROUPED>
