@@ -676,7 +676,7 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tw, const CUtensorMap& tx, c
                                  cudaStream_t st) {
   using C = Cfg<MODE, BN, GROUPED>;
   auto kern = gemm_tc_kernel<MODE, BN, GROUPED>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  cudaError_t e = set_smem_once(kern, C::SMEM);
   if (e != cudaSuccess) return e;
   const int tiles = a.m_tiles * a.n_tiles;
   const int grid = tiles < num_sms() ? tiles : num_sms();

@@ -15,6 +15,8 @@
 #include <stdint.h>
 #include <stdlib.h>
 
+#include <mutex>
+
 #include "../../include/intcrush_b200.h"
 
 #ifndef IC_WAIT_NS
@@ -27,6 +29,33 @@
 __device__ int g_ic_dev_error = 0;
 
 namespace ic {
+
+// Raise a kernel's dynamic shared-memory limit once per device (host side).
+// Later launches, including those recorded into a CUDA graph, make no
+// attribute calls.  Keyed by kernel address; a small lock-protected table.
+inline cudaError_t set_smem_once(const void* kern, int bytes) {
+  struct Entry { const void* k; unsigned long long devs; };
+  static Entry table[256];
+  static int used = 0;
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  std::lock_guard<std::mutex> lock(mu);
+  Entry* e = nullptr;
+  for (int i = 0; i < used; ++i)
+    if (table[i].k == kern) { e = &table[i]; break; }
+  if (e && (e->devs & bit)) return cudaSuccess;
+  cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (r != cudaSuccess) return r;
+  if (!e && used < 256) { e = &table[used++]; e->k = kern; e->devs = 0; }
+  if (e) e->devs |= bit;
+  return cudaSuccess;
+}
+template <typename K>
+inline cudaError_t set_smem_once(K* kern, int bytes) {
+  return set_smem_once(reinterpret_cast<const void*>(kern), bytes);
+}
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;

@@ -1,0 +1,56 @@
+"""The C-ABI library loads without a GPU, exports every entry point declared
+in include/intcrush_b200.h, and rejects bad arguments before touching CUDA."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from _pkg import load
+
+L = load("_lib")
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    src = open(os.path.join(ROOT, "include", "intcrush_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(ic_\w+)\s*\(", src, flags=re.M)))
+
+
+def test_library_loads_and_exports_all_declared_symbols():
+    lib = L.lib()
+    names = declared_functions()
+    assert len(names) >= 10
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared but not exported"
+    assert set(names) <= set(L.SIGNATURES), "every declared entry point has a ctypes signature"
+
+
+def test_version():
+    assert L.lib().ic_version() >> 16 == 1
+
+
+@pytest.mark.parametrize("call,code", [
+    (lambda l: l.ic_gemm_a8(None, 4, 64, 64, None, 7, 8, 32, None, 1, 64, None, None, 0, None, None, None, 0, 8,
+                            None), L.IC_ERR_ARG),
+    (lambda l: l.ic_prep_quant(None, 9, 4, 64, 64, None, 0, 64, None, None, None, 0, None, None, None, None),
+     L.IC_ERR_ARG),
+    (lambda l: l.ic_prep_quant(ctypes.c_void_p(16), 0, 4, 64, 64, None, 48, 64, None, None, None, 0, None, None,
+                               None, None), L.IC_ERR_ARG),
+    (lambda l: l.ic_gemm_w4a16(None, 1, 4, 64, 64, None, 8, 32, 0, None, 0, 1, 64, None, 0, None, None, 0, 1.0,
+                               None, 8, None), L.IC_ERR_UNSUPPORTED),
+    (lambda l: l.ic_repack_int4(None, 4, 64, 32, None, 32, 5, None), L.IC_ERR_ARG),
+    (lambda l: l.ic_lowrank_add(None, 4, 8, 8, None, None, 128, 1.0, None), L.IC_ERR_UNSUPPORTED),
+])
+def test_argument_validation_without_gpu(call, code):
+    lib = L.lib()
+    assert call(lib) == code
+    assert lib.ic_last_error().decode()
+
+
+def test_zero_sized_calls_are_no_ops():
+    lib = L.lib()
+    assert lib.ic_prep_quant(None, 0, 0, 64, 64, None, 0, 64, None, None, None, 0, None, None, None, None) == L.IC_OK
+    assert lib.ic_unpack_int4_to_int8(None, 0, 64, 32, None, None) == L.IC_OK
