@@ -316,9 +316,9 @@ static cudaError_t launch_prep_t(const PrepArgs& a, cudaStream_t st) {
   const size_t xr_elems = (size_t)((a.Wp + 7) & ~7LL);
   const size_t smem = buf_bytes + (xr_elems + (need_xp ? (size_t)a.w_in : 0)) * sizeof(T) + 16;
   auto kern = prep_quant_kernel<T, LOG2R, SYL>;
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  if (smem > 220 * 1024) return cudaErrorInvalidValue;   // dynamic + static shared memory must fit 227 KB
   if (smem > 48 * 1024) {
-    cudaError_t e = set_smem_once(kern, 227 * 1024);
+    cudaError_t e = set_smem_once(kern, 220 * 1024);
     if (e != cudaSuccess) return e;
   }
   kern<<<(unsigned)a.M, kPrepThreads, smem, st>>>(a);

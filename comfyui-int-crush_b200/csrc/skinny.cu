@@ -201,9 +201,9 @@ __global__ void __launch_bounds__(256) lowrank_down_kernel(const __half* x, int 
 cudaError_t launch_lowrank_down(const __half* x, int M, int K, long long ldx, const __half* down, int R,
                                 __half* mid, cudaStream_t st) {
   const size_t smem = (size_t)K * sizeof(__half);
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  if (smem > 220 * 1024) return cudaErrorInvalidValue;   // dynamic + static shared memory must fit 227 KB
   if (smem > 48 * 1024) {
-    cudaError_t e = set_smem_once(lowrank_down_kernel, 227 * 1024);
+    cudaError_t e = set_smem_once(lowrank_down_kernel, 220 * 1024);
     if (e != cudaSuccess) return e;
   }
   lowrank_down_kernel<<<M, 256, smem, st>>>(x, K, ldx, down, R, mid);
