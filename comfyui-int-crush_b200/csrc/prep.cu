@@ -24,6 +24,7 @@
 // per pass; passes exchange through a padded fp64 shared buffer.
 #include "ic_common.cuh"
 
+
 namespace ic {
 
 struct PrepArgs {
@@ -46,12 +47,23 @@ struct PrepArgs {
 
 constexpr int kPrepThreads = 256;
 
+// Elements of a row rotated per block-wide step (a multiple of the rotation
+// size); small enough that several rows fit in one SM's shared memory.
+#ifndef IC_PREP_CHUNK
+#define IC_PREP_CHUNK 1024
+#endif
+template <int LOG2R>
+constexpr int kPrepChunk = (LOG2R == 0) ? 0 : ((1 << LOG2R) > IC_PREP_CHUNK ? (1 << LOG2R) : IC_PREP_CHUNK);
+
 // Padded fp64 index: one pad slot every 16 values keeps the 16-value
 // register blocks of neighbouring threads in different banks.
 __device__ __forceinline__ int pidx(int e) { return e + (e >> 4); }
 
-template <int L, bool SYL>
-__device__ __forceinline__ void butterflies(double (&v)[1 << L]) {
+// Rotation arithmetic type: fp64 (exact for sums of fp16 values, see above).
+template <typename T> struct RotT { using V = double; };
+
+template <int L, bool SYL, typename V>
+__device__ __forceinline__ void butterflies(V (&v)[1 << L]) {
   constexpr int N = 1 << L;
   if constexpr (SYL) {
 #pragma unroll
@@ -60,7 +72,7 @@ __device__ __forceinline__ void butterflies(double (&v)[1 << L]) {
 #pragma unroll
       for (int i = 0; i < N; ++i) {
         if ((i & h) == 0) {
-          const double a = v[i], b = v[i + h];
+          const V a = v[i], b = v[i + h];
           v[i] = a + b;
           v[i + h] = a - b;
         }
@@ -73,12 +85,12 @@ __device__ __forceinline__ void butterflies(double (&v)[1 << L]) {
 #pragma unroll
       for (int i = 0; i < N; ++i) {
         if (((i >> (2 * d)) & 3) == 0) {
-          const double a0 = v[i], a1 = v[i + st], a2 = v[i + 2 * st], a3 = v[i + 3 * st];
-          const double s = (a0 + a1) + (a2 + a3);
-          v[i] = s - 2.0 * a3;
-          v[i + st] = s - 2.0 * a2;
-          v[i + 2 * st] = s - 2.0 * a1;
-          v[i + 3 * st] = s - 2.0 * a0;
+          const V a0 = v[i], a1 = v[i + st], a2 = v[i + 2 * st], a3 = v[i + 3 * st];
+          const V s = (a0 + a1) + (a2 + a3);
+          v[i] = s - (a3 + a3);
+          v[i + st] = s - (a2 + a2);
+          v[i + 2 * st] = s - (a1 + a1);
+          v[i + 3 * st] = s - (a0 + a0);
         }
       }
     }
@@ -97,9 +109,11 @@ __device__ __forceinline__ float load_x(const PrepArgs& a, const T* xrow, int64_
   return v;
 }
 
+template <typename V, typename T> __device__ __forceinline__ V to_rot(float f) { return (V)f; }
+
 // Load 16 consecutive inputs starting at k0 (vectorised when legal).
-template <typename T>
-__device__ __forceinline__ void load16(const PrepArgs& a, const T* xrow, int64_t k0, double (&v)[16]) {
+template <typename T, typename V>
+__device__ __forceinline__ void load16(const PrepArgs& a, const T* xrow, int64_t k0, V (&v)[16]) {
   if (a.vec_ok && k0 + 16 <= a.K) {
     const uint4* p = reinterpret_cast<const uint4*>(xrow + k0);
     uint4 q0 = __ldg(p), q1 = __ldg(p + 1);
@@ -114,12 +128,12 @@ __device__ __forceinline__ void load16(const PrepArgs& a, const T* xrow, int64_t
         f0 = DT<T>::to_f(DT<T>::from_f(__fdiv_rn(f0, s0)));
         f1 = DT<T>::to_f(DT<T>::from_f(__fdiv_rn(f1, s1)));
       }
-      v[j] = f0;
-      v[8 + j] = f1;
+      v[j] = to_rot<V, T>(f0);
+      v[8 + j] = to_rot<V, T>(f1);
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = load_x<T>(a, xrow, k0 + j);
+    for (int j = 0; j < 16; ++j) v[j] = to_rot<V, T>(load_x<T>(a, xrow, k0 + j));
   }
 }
 
@@ -153,7 +167,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 // index bits [S, S + L) of each rotation group of size 2^LOG2R.
 template <typename T, int LOG2R, bool SYL, int S, int L, bool FIRST, bool LAST>
 __device__ __forceinline__ void rot_pass(const PrepArgs& a, const T* xrow, int c0, int CH,
-                                         double* buf, T* xr) {
+                                         typename RotT<T>::V* buf, T* xr) {
+  using V = typename RotT<T>::V;
   constexpr int R = 1 << LOG2R;
   constexpr int E = 1 << L;
   constexpr int HIGH = R >> (S + L);
@@ -164,27 +179,27 @@ __device__ __forceinline__ void rot_pass(const PrepArgs& a, const T* xrow, int c
     const int high = rest % HIGH;
     const int g = rest / HIGH;
     const int base = g * R + low + (high << (S + L));
-    double v[E];
+    V v[E];
     if constexpr (FIRST) {
       static_assert(S == 0, "first pass starts at bit 0");
       if constexpr (E == 16) {
-        load16<T>(a, xrow, (int64_t)c0 + base, v);
+        load16<T, V>(a, xrow, (int64_t)c0 + base, v);
       } else {
 #pragma unroll
-        for (int j = 0; j < E; ++j) v[j] = load_x<T>(a, xrow, (int64_t)c0 + base + j);
+        for (int j = 0; j < E; ++j) v[j] = to_rot<V, T>(load_x<T>(a, xrow, (int64_t)c0 + base + j));
       }
     } else {
 #pragma unroll
       for (int j = 0; j < E; ++j) v[j] = buf[pidx(base + (j << S))];
     }
-    butterflies<L, SYL>(v);
+    butterflies<L, SYL, V>(v);
     if constexpr (LAST) {
 #pragma unroll
       for (int j = 0; j < E; ++j) {
-        double y;
-        if constexpr (SYL) y = v[j] * a.syl_h;
-        else y = v[j] * (1.0 / (double)(1 << (LOG2R / 2)));   // 2^-D, exact
-        xr[c0 + base + (j << S)] = DT<T>::from_d(y);
+        T out;
+        if constexpr (SYL) out = DT<T>::from_d(v[j] * a.syl_h);
+        else out = DT<T>::from_d(v[j] * (1.0 / (double)(1 << (LOG2R / 2))));   // 2^-D, exact
+        xr[c0 + base + (j << S)] = out;
       }
     } else {
 #pragma unroll
@@ -195,7 +210,7 @@ __device__ __forceinline__ void rot_pass(const PrepArgs& a, const T* xrow, int c
 
 template <typename T, int LOG2R, bool SYL, int S>
 __device__ __forceinline__ void rot_passes(const PrepArgs& a, const T* xrow, int c0, int CH,
-                                           double* buf, T* xr) {
+                                           typename RotT<T>::V* buf, T* xr) {
   // bits per pass: 4 (two radix-4 digits / four radix-2 stages); the last
   // pass takes what is left (2 for an odd digit count of a regular size).
   constexpr int REM = LOG2R - S;
@@ -216,9 +231,9 @@ __global__ void __launch_bounds__(kPrepThreads) prep_quant_kernel(const PrepArgs
   const int64_t row = blockIdx.x;
   const T* xrow = reinterpret_cast<const T*>(a.x) + row * a.ldx;
 
-  // layout: [fp64 rotation buffer][xr: Wp values of T][xp: w_in values of T]
-  constexpr int CH = (LOG2R == 0) ? 0 : ((1 << LOG2R) > 1024 ? (1 << LOG2R) : 1024);
-  double* buf = reinterpret_cast<double*>(smem);
+  // layout: [64-bit rotation buffer][xr: Wp values of T][xp: w_in values of T]
+  constexpr int CH = kPrepChunk<LOG2R>;
+  typename RotT<T>::V* buf = reinterpret_cast<typename RotT<T>::V*>(smem);
   const int buf_bytes = (LOG2R > 4) ? ((CH + CH / 16) * 8) : 0;
   T* xr = reinterpret_cast<T*>(smem + buf_bytes);
   const int Wp = (int)a.Wp, w_in = (int)a.w_in;
@@ -248,18 +263,37 @@ __global__ void __launch_bounds__(kPrepThreads) prep_quant_kernel(const PrepArgs
   for (int k = (int)a.Kr + threadIdx.x; k < Wp; k += kPrepThreads) xr[k] = DT<T>::from_f(0.f);
   __syncthreads();
 
-  // 2. gather + SmoothQuant divide into xp, row absmax (and sum)
+  // 2. gather + SmoothQuant divide into xp, row absmax (and sum).  Four
+  // consecutive outputs per thread per step with 16-byte index / factor loads,
+  // unrolled so that the global (L2) loads of all steps are in flight at once.
   float amax = 0.f, rsum = 0.f;
-  for (int j = threadIdx.x; j < w_in; j += kPrepThreads) {
-    T v = xr[a.perm ? a.perm[j] : j];
-    if (a.smooth) {
-      const float f = DT<T>::to_f(DT<T>::from_f(a.smooth[j]));
-      v = DT<T>::from_f(__fdiv_rn(DT<T>::to_f(v), f));
-    }
+  const bool vec4 = ((w_in & 3) == 0) &&
+                    ((reinterpret_cast<uintptr_t>(a.perm) | reinterpret_cast<uintptr_t>(a.smooth)) & 15) == 0;
+  auto one = [&](int j, int src, float f_s) {
+    T v = xr[src];
+    if (a.smooth) v = DT<T>::from_f(__fdiv_rn(DT<T>::to_f(v), f_s));
     if (need_xp) xp[j] = v;
     const float fv = DT<T>::to_f(v);
     amax = fmaxf(amax, fabsf(fv));
     rsum += fv;
+  };
+  if (vec4) {
+#pragma unroll 4
+    for (int j0 = threadIdx.x * 4; j0 < w_in; j0 += kPrepThreads * 4) {
+      int4 src = make_int4(j0, j0 + 1, j0 + 2, j0 + 3);
+      if (a.perm) src = __ldg(reinterpret_cast<const int4*>(a.perm + j0));
+      float4 sm = make_float4(1.f, 1.f, 1.f, 1.f);
+      if (a.smooth) sm = __ldg(reinterpret_cast<const float4*>(a.smooth + j0));
+      const float f0 = DT<T>::to_f(DT<T>::from_f(sm.x)), f1 = DT<T>::to_f(DT<T>::from_f(sm.y));
+      const float f2 = DT<T>::to_f(DT<T>::from_f(sm.z)), f3 = DT<T>::to_f(DT<T>::from_f(sm.w));
+      one(j0, src.x, f0);
+      one(j0 + 1, src.y, f1);
+      one(j0 + 2, src.z, f2);
+      one(j0 + 3, src.w, f3);
+    }
+  } else {
+    for (int j = threadIdx.x; j < w_in; j += kPrepThreads)
+      one(j, a.perm ? a.perm[j] : j, a.smooth ? DT<T>::to_f(DT<T>::from_f(a.smooth[j])) : 1.f);
   }
   amax = block_max(amax, red);
   if (a.rowsum) {
@@ -283,6 +317,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_quant_kernel(const PrepArgs
   // 4. quantise: s = max(amax, 1e-8) / 127, q = clamp(rint(x / s))
   if (a.xq) {
     const float s = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
+    const float rs = __frcp_rn(s);
     if (threadIdx.x == 0) a.s_a[row] = s;
     int8_t* qrow = a.xq + row * a.ldq;
     const int ldq = (int)a.ldq;
@@ -296,8 +331,17 @@ __global__ void __launch_bounds__(kPrepThreads) prep_quant_kernel(const PrepArgs
           const int j = j0 + w * 4 + b;
           int q = 0;
           if (j < w_in) {
-            const float r = rintf(__fdiv_rn(DT<T>::to_f(xp[j]), s));
-            q = (int)fminf(fmaxf(r, -128.f), 127.f);
+            // q = rint(x / s) with the quotient correctly rounded to fp32.
+            // x * (1/s) is within 2 fp32 ulps of that quotient, so it rounds
+            // to the same integer unless it lies within 2^-21 (relative) of
+            // a half-integer; only then is the exact division evaluated.
+            // Adding 1.5 * 2^23 rounds to the nearest integer, ties to even
+            // (|x / s| <= 127.x), leaving it in the low mantissa bits.
+            const float xv = DT<T>::to_f(xp[j]);
+            float y = xv * rs;
+            const float fy = fabsf(y);
+            if (fabsf(fy - (floorf(fy) + 0.5f)) <= fy * 4.8e-7f) y = __fdiv_rn(xv, s);
+            q = max(-128, min(127, __float_as_int(y + 12582912.0f) - 0x4B400000));
           }
           word |= ((uint32_t)(q & 0xFF)) << (8 * b);
         }
@@ -310,7 +354,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_quant_kernel(const PrepArgs
 
 template <typename T, int LOG2R, bool SYL>
 static cudaError_t launch_prep_t(const PrepArgs& a, cudaStream_t st) {
-  constexpr int CH = (LOG2R == 0) ? 0 : ((1 << LOG2R) > 1024 ? (1 << LOG2R) : 1024);
+  constexpr int CH = kPrepChunk<LOG2R>;
   const int buf_bytes = (LOG2R > 4) ? ((CH + CH / 16) * 8) : 0;
   const bool need_xp = (a.perm != nullptr) || (a.smooth != nullptr);
   const size_t xr_elems = (size_t)((a.Wp + 7) & ~7LL);
