@@ -276,6 +276,26 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def kernel_probe(which: str) -> None:
+    """Three launches of one kernel of the config-2 step (for ncu captures)."""
+    import torch
+    rt = _pkg()
+    dev = torch.device("cuda")
+    d = make_inputs(device=dev)
+    perm32 = d["perm"].to(torch.int32)
+    w_rep = rt.repack_int4(d["packed"], K, 0)
+    s_w = d["scale"].float()
+    xq, s_a, _, _ = rt.prep_quantize(d["x"], smoothrot=d["smoothrot"], rot_size=ROT, w_in=K, perm=perm32)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        if which == "prep":
+            rt.prep_quantize(d["x"], smoothrot=d["smoothrot"], rot_size=ROT, w_in=K, perm=perm32)
+        else:
+            rt.gemm_a8(xq, w_rep, s_w, s_a, bias=d["bias"], out_dtype=torch.float16, group_size=GS, repacked=True)
+    torch.cuda.synchronize()
+    assert rt.device_error() == 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -283,7 +303,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--kernel-probe", choices=["prep", "gemm"], default=None,
+                    help="run only this kernel of the step (3 launches) for profiling; prints nothing")
     args = ap.parse_args()
+    if args.kernel_probe:
+        kernel_probe(args.kernel_probe)
+        return
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
