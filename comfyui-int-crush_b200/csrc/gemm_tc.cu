@@ -85,16 +85,21 @@ struct Cfg {
   static constexpr int W_BYTES = kTileN * 128;                    // 16 KB
   static constexpr int X_BYTES = BN * 128;
   static constexpr int P_BYTES = (MODE == W_I4) ? kTileN * 64 : (MODE == W_I4F ? kTileN * 32 : 0);
-  static constexpr int BUDGET = 224 * 1024;
+  // group-scaled tiles: four accumulator buffers when they fit in TMEM, and
+  // two 1 KB constant atoms (the operands of the re-arming MMA) at offset 0
+  static constexpr int NBUF = (GROUPED && BN <= 128) ? 4 : 2;
+  static constexpr int MAGIC_BYTES = GROUPED ? 2048 : 0;
+  static constexpr int BUDGET = 224 * 1024 - MAGIC_BYTES;
   static constexpr int S_P = I4 ? 8 : 0;   // even: the two expansion warps own alternate stages
   static constexpr int S_W = I4 ? 4 : 0;
   static constexpr int XSTAGE = I4 ? X_BYTES : (X_BYTES + W_BYTES);
   static constexpr int S_X_RAW = (BUDGET - S_P * P_BYTES - S_W * W_BYTES) / XSTAGE;
   static constexpr int S_X = S_X_RAW > 6 ? 6 : S_X_RAW;
-  static constexpr int OFF_W = S_X * XSTAGE;                      // W ring (I4)
+  static constexpr int OFF_X = MAGIC_BYTES;                       // X ring
+  static constexpr int OFF_W = OFF_X + S_X * XSTAGE;              // W ring (I4)
   static constexpr int OFF_P = OFF_W + S_W * W_BYTES;             // P ring (I4)
   static constexpr int OFF_BAR = OFF_P + S_P * P_BYTES;
-  static constexpr int TMEM_COLS_RAW = 2 * BN;
+  static constexpr int TMEM_COLS_RAW = NBUF * BN;
   static constexpr int TMEM_COLS = TMEM_COLS_RAW <= 32 ? 32 : TMEM_COLS_RAW <= 64 ? 64
                                  : TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
   static constexpr int SMEM = OFF_BAR + 512 + 1024;               // barriers + alignment slack
@@ -105,6 +110,7 @@ struct Cfg {
   static_assert(S_X >= 2, "pipeline depth");
   static_assert(!(GROUPED && MODE == W_I4F), "W4A16 folds scales into the weights");
   static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(TMEM_COLS_RAW <= 512, "tensor memory");
 };
 
 // Nibble pairs -> int8 bytes holding 16*q (two's complement nibble in the
@@ -248,9 +254,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   uint64_t* w_full = bars + 2 * SX;           // [SW] expansion -> MMA (I4)
   uint64_t* w_empty = w_full + SW;            // [SW] MMA commit -> expansion (I4)
   uint64_t* p_full = w_empty + SW;            // [SP] TMA -> expansion (I4)
-  uint64_t* acc_full = p_full + SP;           // [2] MMA commit -> epilogue
-  uint64_t* acc_empty = acc_full + 2;         // [2] epilogue -> MMA (count EPI)
-  uint64_t* drain = acc_empty + 2;            // abort path: MMA completion
+  constexpr int NB = C::NBUF;
+  uint64_t* acc_full = p_full + SP;           // [NB] MMA commit -> epilogue
+  uint64_t* acc_empty = acc_full + NB;        // [NB] epilogue -> MMA (count EPI)
+  uint64_t* drain = acc_empty + NB;           // abort path: MMA completion
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 2);
 
@@ -267,7 +274,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       mbar_init(&w_empty[s], 1);
     }
     for (int s = 0; s < SP; ++s) mbar_init(&p_full[s], 1);
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NB; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], C::EPI);
     }
@@ -283,6 +290,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     prefetch_tmap(&tm_w);
     prefetch_tmap(&tm_x);
   }
+  if constexpr (GROUPED) {
+    // Constant operands of the re-arming MMA: every fp16 of atom A is 1536,
+    // every fp16 of atom B is 512, so a K = 16 product is 16 * 1536 * 512 =
+    // 1.5 * 2^23 exactly, whose fp32 bits are the magic 0x4B400000.
+    uint32_t* m = reinterpret_cast<uint32_t*>(smem);
+    for (int i = threadIdx.x; i < 512; i += blockDim.x) m[i] = (i < 256) ? 0x66006600u : 0x60006000u;
+    fence_proxy_async_smem();
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -291,9 +306,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   const int total_tiles = a.m_tiles * a.n_tiles;
   const int units = GROUPED ? a.G : 1;
 
-  auto x_stage = [&](int s) { return smem + s * C::XSTAGE + (C::I4 ? 0 : C::W_BYTES); };
+  auto x_stage = [&](int s) { return smem + C::OFF_X + s * C::XSTAGE + (C::I4 ? 0 : C::W_BYTES); };
   auto w_stage = [&](int s) {
-    return C::I4 ? smem + C::OFF_W + s * C::W_BYTES : smem + s * C::XSTAGE;
+    return C::I4 ? smem + C::OFF_W + s * C::W_BYTES : smem + C::OFF_X + s * C::XSTAGE;
   };
   auto p_stage = [&](int s) { return smem + C::OFF_P + s * C::P_BYTES; };
 
@@ -325,18 +340,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = (MODE == W_I4F) ? idesc_f16(kTileN, BN, false) : idesc_i8(kTileN, BN);
+      // GROUPED: the re-arming MMA (kind::f16, K = 16, accumulate off) writes
+      // 1.5 * 2^23 as fp32 into every element of the buffer; the group's
+      // kind::i8 MMAs then add the int32 partial onto those bits.  SBO = 0 makes
+      // all 8-row groups of an operand read the same 1 KB atom.
+      const uint32_t idesc_m = idesc_f16(kTileN, BN, false);
+      const uint64_t magic_a = smem_desc_sw128(smem_u32(smem)) & ~(0x3FFFull << 32);
+      const uint64_t magic_b = smem_desc_sw128(smem_u32(smem + 1024)) & ~(0x3FFFull << 32);
       int it = 0, uc = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
         for (int u = 0; ok && u < units; ++u, ++uc) {
           const int kb0 = GROUPED ? u * a.kb_per_group : 0;
           const int kb1 = GROUPED ? min(kb0 + a.kb_per_group, a.num_kb) : a.num_kb;
-          const int b = uc & 1;
+          const int b = uc % NB;
           { IC_T0();
-          if (!mbar_wait(&acc_empty[b], (uint32_t)(uc >> 1) & 1u, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&acc_empty[b], (uint32_t)(uc / NB) & 1u, abort_flag)) { ok = false; break; }
           IC_TADD(0); }
           tc_fence_after();
           const uint32_t d = tmem_base + (uint32_t)(b * BN);
+          if constexpr (GROUPED) mma_f16(d, magic_a, magic_b, idesc_m, 0u);
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int sx = it % SX;
             { IC_T0();
@@ -412,43 +435,67 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
           uint8_t* W = w_stage(sw);
           const uint8_t* P = p_stage(sp);
+#if !defined(IC_DIAG_NOEXPAND)   // tuning-only: measure the pipeline without the expansion work
           if constexpr (MODE == W_I4) {
-#pragma unroll 4
-            for (int i = 0; i < 16; ++i) {
-              const int r = i * 8 + (lane >> 2), c = lane & 3;
-              const uint4 p = *reinterpret_cast<const uint4*>(P + r * 64 + c * 16);
-              uint4 o0, o1;
-              if (rp) {
+            // all sixteen 16-byte loads first: one shared-memory latency per
+            // stage instead of one per few rows
+            const int c = lane & 3;
+            uint4 pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              pk[i] = *reinterpret_cast<const uint4*>(P + (i * 8 + (lane >> 2)) * 64 + c * 16);
+            if (rp) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
                 // layout 0: byte b of a word = q[k_b] | q[k_{b+4}] << 4
+                const uint4 p = pk[i];
+                const int r = i * 8 + (lane >> 2);
+                uint4 o0, o1;
                 o0.x = (p.x << 4) & 0xF0F0F0F0u; o0.y = p.x & 0xF0F0F0F0u;
                 o0.z = (p.y << 4) & 0xF0F0F0F0u; o0.w = p.y & 0xF0F0F0F0u;
                 o1.x = (p.z << 4) & 0xF0F0F0F0u; o1.y = p.z & 0xF0F0F0F0u;
                 o1.z = (p.w << 4) & 0xF0F0F0F0u; o1.w = p.w & 0xF0F0F0F0u;
-              } else {
+                *reinterpret_cast<uint4*>(W + sw128_offset(r, 2 * c)) = o0;
+                *reinterpret_cast<uint4*>(W + sw128_offset(r, 2 * c + 1)) = o1;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const uint4 p = pk[i];
+                const int r = i * 8 + (lane >> 2);
+                uint4 o0, o1;
                 expand_i4_i8(p.x, o0.x, o0.y);
                 expand_i4_i8(p.y, o0.z, o0.w);
                 expand_i4_i8(p.z, o1.x, o1.y);
                 expand_i4_i8(p.w, o1.z, o1.w);
+                *reinterpret_cast<uint4*>(W + sw128_offset(r, 2 * c)) = o0;
+                *reinterpret_cast<uint4*>(W + sw128_offset(r, 2 * c + 1)) = o1;
               }
-              *reinterpret_cast<uint4*>(W + sw128_offset(r, 2 * c)) = o0;
-              *reinterpret_cast<uint4*>(W + sw128_offset(r, 2 * c + 1)) = o1;
             }
           } else {
             const int g = (a.G > 1) ? (kb * 64) / a.group_size : 0;
-#pragma unroll 2
+            const int c = lane & 1;
+            // scales and packed words of the lane's eight rows, all loads first
+            __half sh[8];
+            uint4 pk[8];
+#pragma unroll
             for (int i = 0; i < 8; ++i) {
-              const int r = i * 16 + (lane >> 1), c = lane & 1;
+              const int r = i * 16 + (lane >> 1);
               const int n = n_blk * kTileN + r;
-              __half sh = __float2half_rn(0.f);
+              sh[i] = __float2half_rn(0.f);
               if (n < a.N) {
                 const size_t si = (size_t)n * a.G + g;
-                sh = (a.w_scale_dtype == IC_DTYPE_F16)
-                         ? reinterpret_cast<const __half*>(a.w_scale)[si]
-                         : __float2half_rn(reinterpret_cast<const float*>(a.w_scale)[si]);
+                sh[i] = (a.w_scale_dtype == IC_DTYPE_F16)
+                            ? reinterpret_cast<const __half*>(a.w_scale)[si]
+                            : __float2half_rn(reinterpret_cast<const float*>(a.w_scale)[si]);
               }
-              const __half2 s2 = __half2half2(sh);
-              const uint4 p = *reinterpret_cast<const uint4*>(P + r * 32 + c * 16);
-              const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
+              pk[i] = *reinterpret_cast<const uint4*>(P + r * 32 + c * 16);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = i * 16 + (lane >> 1);
+              const __half2 s2 = __half2half2(sh[i]);
+              const uint32_t pw[4] = {pk[i].x, pk[i].y, pk[i].z, pk[i].w};
 #pragma unroll
               for (int w = 0; w < 4; ++w) {
                 uint4 o;
@@ -469,9 +516,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
               }
             }
           }
-          fence_proxy_async_smem();
+#endif
+#if defined(IC_TRACE)
           __syncwarp();
           if (lane == 0) IC_TADD(7);
+          _t0 = clock64();
+#endif
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) IC_TADD(9);
           if (lane == 0) {
             mbar_arrive(&w_full[sw]);
             issue_p(it + SP);   // same parity as it: this warp's next use of the stage
@@ -491,20 +544,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     const int col0 = (e >> 2) * C::CPT;
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
     constexpr float wmul = (MODE == W_I4) ? 0.0625f : 1.0f;   // int4 held as 16*q
-    if constexpr (GROUPED) {
-#pragma unroll
-      for (int b = 0; b < 2; ++b)
-#pragma unroll
-        for (int c = 0; c < C::CPT / 16; ++c)
-          tmem_st16_const(tmem_base + lane_base + (uint32_t)(b * BN + col0 + 16 * c), kMagic);
-      tmem_wait_st();
-    }
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(&acc_empty[0]);
-      mbar_arrive(&acc_empty[1]);
-    }
+    if (lane == 0)
+      for (int b = 0; b < NB; ++b) mbar_arrive(&acc_empty[b]);
     int uc = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
@@ -522,58 +565,32 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         const float* swrow = a.s_w + (size_t)(nvalid ? n : 0) * a.G;
         float sw = nvalid ? __ldg(swrow) * wmul : 0.f;
         for (int u = 0; u < units; ++u, ++uc) {
-          const int b = uc & 1;
+          const int b = uc % NB;
           // next group's scale is fetched while this group is consumed
           const float sw_next = (nvalid && u + 1 < units) ? __ldg(swrow + u + 1) * wmul : 0.f;
           IC_T0();
-          if (!mbar_wait(&acc_full[b], (uint32_t)(uc >> 1) & 1u, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&acc_full[b], (uint32_t)(uc / NB) & 1u, abort_flag)) { ok = false; break; }
           if (warp == 4 && lane == 0) IC_TADD(3);
 #if defined(IC_TRACE)
           _t0 = clock64();
           if (warp == 4 && lane == 0) atomicAdd(&g_ic_trace[10], 1ull);
 #endif
           tc_fence_after();
-          const unsigned long long sw2 = pack2(sw, sw);
-#if defined(IC_EPI_SINGLE_WAIT)
-          {
-            uint32_t r[C::CPT / 16][16];
+          // read the whole buffer, then hand it back at once: the MMA warp
+          // re-arms it itself, so nothing is written to tensor memory here
+          uint32_t r[C::CPT / 32][32];
 #pragma unroll
-            for (int c = 0; c < C::CPT / 16; ++c)
-              tmem_ld16(tmem_base + lane_base + (uint32_t)(b * BN + col0 + 16 * c), r[c]);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < C::CPT / 16; ++c)
-              tmem_st16_const(tmem_base + lane_base + (uint32_t)(b * BN + col0 + 16 * c), kMagic);
-#pragma unroll
-            for (int c = 0; c < C::CPT / 16; ++c)
-#pragma unroll
-              for (int j = 0; j < 8; ++j) acc2p(accp[8 * c + j], r[c][2 * j], r[c][2 * j + 1], sw2, mg2);
-          }
-#else
-#pragma unroll
-          for (int c = 0; c < C::CPT / 16; ++c) {
-            const uint32_t ta = tmem_base + lane_base + (uint32_t)(b * BN + col0 + 16 * c);
-            uint32_t r[16];
-            tmem_ld16(ta, r);
-            tmem_wait_ld();
-            tmem_st16_const(ta, kMagic);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-#if defined(IC_EPI_SCALAR)
-              float lo = __uint_as_float((uint32_t)accp[8 * c + j]), hi = __uint_as_float((uint32_t)(accp[8 * c + j] >> 32));
-              lo = fmaf(__uint_as_float(r[2 * j]) - kMagicF, sw, lo);
-              hi = fmaf(__uint_as_float(r[2 * j + 1]) - kMagicF, sw, hi);
-              accp[8 * c + j] = pack2(lo, hi);
-#else
-              acc2p(accp[8 * c + j], r[2 * j], r[2 * j + 1], sw2, mg2);
-#endif
-            }
-          }
-#endif
-          tmem_wait_st();
+          for (int c = 0; c < C::CPT / 32; ++c)
+            tmem_ld32(tmem_base + lane_base + (uint32_t)(b * BN + col0 + 32 * c), r[c]);
+          tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[b]);
+          const unsigned long long sw2 = pack2(sw, sw);
+#pragma unroll
+          for (int c = 0; c < C::CPT / 32; ++c)
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc2p(accp[16 * c + j], r[c][2 * j], r[c][2 * j + 1], sw2, mg2);
           if (warp == 4 && lane == 0) IC_TADD(4);
           sw = sw_next;
         }
@@ -589,9 +606,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           store_chunk(a, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane);
         }
       } else {
-        const int b = uc & 1;
+        const int b = uc % NB;
         const float sw = (MODE == W_I4F) ? 1.f : (nvalid ? __ldg(&a.s_w[n]) * wmul : 0.f);
-        if (!mbar_wait(&acc_full[b], (uint32_t)(uc >> 1) & 1u, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&acc_full[b], (uint32_t)(uc / NB) & 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < C::CPT / 32; ++c) {
