@@ -276,6 +276,67 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_features(args, rank: int, world: int, local_rank: int) -> None:
+    """Output-feature-sharded layer: every rank holds N / world weight rows,
+    preps the same 4096 tokens, runs its GEMM slice, and an NCCL all-gather
+    assembles the [M, N] output (strong scaling: total work fixed)."""
+    import torch
+    import torch.distributed as dist
+    rt = _pkg()
+    import importlib
+    sh = importlib.import_module(PKG + "._sharded")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    d = make_inputs(seed=0, device=dev)          # the same layer and tokens on every rank
+    lin = sh.FeatureShardedLinear(d["packed"], d["scale"], d["bias"], group_size=GS, smoothrot=d["smoothrot"],
+                                  rot_size=ROT, w_in=K, perm=d["perm"], device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    st = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        lin(d["x"])
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local_rank) as clk:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            ev[i][0].record(st)
+            local = lin.local_forward(d["x"], torch.float16)
+            ev[i][1].record(st)
+            if world > 1:
+                parts = [torch.empty_like(local) for _ in range(world)]
+                dist.all_gather(parts, local)
+                torch.cat(parts, dim=1)
+            ev[i][2].record(st)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    tot = sum(ev[i][0].elapsed_time(ev[i][2]) for i in range(args.steps))
+    comp = sum(ev[i][0].elapsed_time(ev[i][1]) for i in range(args.steps))
+    vals = torch.tensor([tot, comp], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    tot, comp = vals.tolist()
+    if rank != 0:
+        return
+    ms_step = tot / args.steps
+    line = {
+        "metric": "w4a8_linear_tops", "value": OPS / (ms_step * 1e-3) / 1e12, "unit": "TOPS",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic",
+        "config": {"workload": "config2_w4a8_linear M4096 K3072 N12288 g128 rot256 perm smoothrot bias",
+                   "parallelism": f"output-feature-sharded x{world} + NCCL all-gather",
+                   "l2": "flushed (256 MB write) between timed steps"},
+        "compute_ms_per_step": comp / args.steps,
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def kernel_probe(which: str) -> None:
     """Three launches of one kernel of the config-2 step (for ncu captures)."""
     import torch
@@ -303,6 +364,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--shard", choices=["tokens", "features"], default="tokens",
+                    help="tokens: every rank runs its own 4096 tokens (default); "
+                         "features: one layer split by output features + all-gather")
     ap.add_argument("--kernel-probe", choices=["prep", "gemm"], default=None,
                     help="run only this kernel of the step (3 launches) for profiling; prints nothing")
     args = ap.parse_args()
@@ -322,7 +386,7 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120))
     try:
-        run_gpu(args, rank, world, local_rank)
+        (run_features if args.shard == "features" else run_gpu)(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -1,0 +1,113 @@
+"""Multi-rank layouts on CPU: world_size 2 over gloo.
+
+The GEMM itself is CUDA-only, so these tests give ``FeatureShardedLinear``
+CPU stand-ins for the prep and GEMM callables (the numpy oracle) and check
+the sharding logic: which weight rows each rank keeps, the padding of the
+last rank, the all-gather and the column order of the assembled output, and
+that the assembled output equals the single-process forward exactly.
+"""
+
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import intcrush_oracle as O
+from _pkg import load
+
+sh = load("_sharded")
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _oracle_prep(x, *, smoothrot=None, rot_size=0, w_in=None, perm=None, smooth=None):
+    xp = O.prep_activation(x.numpy(), smoothrot=None if smoothrot is None else smoothrot.numpy(),
+                           rot_need=rot_size > 0, rot_size=rot_size, w_in=w_in,
+                           perm=None if perm is None else perm.numpy(),
+                           smooth=None if smooth is None else smooth.numpy())
+    q, s = O.quantize_rows(xp)
+    return torch.from_numpy(q), torch.from_numpy(s), None, None
+
+
+def _oracle_gemm(xq, w, s_w, s_a, *, bias=None, out_dtype=torch.float32, group_size=None):
+    wq = O.unpack_int4(w.numpy(), xq.shape[1]) if w.dtype == torch.uint8 else w.numpy()
+    sw = s_w.numpy()
+    y = O.gemm_a8(xq.numpy(), s_a.numpy(), wq, sw if sw.shape[1] > 1 else sw[:, 0],
+                  bias=None if bias is None else bias.float().numpy(), group_size=group_size)
+    return torch.from_numpy(y.astype(np.float32)).to(out_dtype)
+
+
+def _case(N, seed=3):
+    rng = np.random.default_rng(seed)
+    M, K, G = 6, 256, 2
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float16))
+    q = rng.integers(-8, 8, (N, K)).astype(np.int8)
+    w = torch.from_numpy(O.pack_int4(q))
+    s_w = torch.from_numpy(rng.uniform(1e-3, 2e-2, (N, G)).astype(np.float32))
+    bias = torch.from_numpy((rng.standard_normal(N) * 0.02).astype(np.float16))
+    sr = torch.from_numpy(rng.uniform(0.5, 4, K).astype(np.float16))
+    perm = torch.from_numpy(rng.permutation(K).astype(np.int32))
+    return x, w, s_w, bias, sr, perm
+
+
+def _worker(rank, world, port, N, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        x, w, s_w, bias, sr, perm = _case(N)
+        lin = sh.FeatureShardedLinear(w, s_w, bias, group_size=128, smoothrot=sr, rot_size=64, w_in=256,
+                                      perm=perm, prep=_oracle_prep, gemm=_oracle_gemm)
+        y = lin(x.to(torch.float32))
+        out_q.put((rank, lin.weight.shape[0], y.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("N", [256, 200])
+def test_feature_sharded_matches_single_process(N):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, N, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    x, w, s_w, bias, sr, perm = _case(N)
+    xq, s_a, _, _ = _oracle_prep(x, smoothrot=sr, rot_size=64, w_in=256, perm=perm)
+    ref = _oracle_gemm(xq, w, s_w, s_a, bias=bias, out_dtype=torch.float32, group_size=128).numpy()
+    for rank, rows, y in res:
+        assert rows == -(-N // world)            # padded per-rank width
+        assert y.shape == (6, N)
+        np.testing.assert_array_equal(y, ref)    # same computation per element
+
+
+def test_feature_rows_cover_once():
+    for N in (1, 7, 128, 12288, 12289):
+        for world in (1, 2, 3, 8):
+            seen = []
+            for r in range(world):
+                a, b, nr = sh.feature_rows(N, r, world)
+                assert 0 <= b - a <= nr
+                seen.extend(range(a, b))
+            assert seen == list(range(N))
+
+
+def test_shard_tokens_cover_once():
+    x = torch.arange(11 * 3).reshape(11, 3)
+    parts = [sh.shard_tokens(x, r, 4) for r in range(4)]
+    assert torch.equal(torch.cat(parts), x)
