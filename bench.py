@@ -13,7 +13,8 @@ Metric: linear TOPS = 2*M*N*K / step time (higher is better).
   ranks (weak scaling: every rank runs its own 4096 tokens; no collective).
 * ``e2e``: the same step through the runtime API with the input copied from
   pinned host memory and the output copied back to pinned host memory inside
-  the timed region.
+  the timed region; copies in, compute and copies out run on three streams so
+  that consecutive steps overlap (the output copy over PCIe bounds it).
 * ``roofline``: the GEMM kernel's algorithmic ops / its event time against the
   dense INT8 peak (2 x the measured bf16 cuBLAS figure); prep against HBM.
 * ``cpu_baseline``: the reference's PyTorch CPU path (torch restatement,
@@ -145,13 +146,30 @@ class Clocks:
                 ["nvidia-smi", "-i", str(self.idx), "--query-gpu=clocks.sm,clocks.max.sm,power.draw,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "--format=csv,noheader,nounits", "-lms", "20"], stdout=self.f, stderr=subprocess.DEVNULL)
+            # the sampler needs a moment to start: wait for its first row so that
+            # short timed regions are covered too
+            t0 = time.time()
+            while time.time() - t0 < 5 and self._rows() < 1:
+                time.sleep(0.01)
+            self.n0 = self._rows()
         except Exception:
             self.proc = None
         return self
 
+    def _rows(self) -> int:
+        try:
+            with open(self.path) as f:
+                return sum(1 for r in f if r.strip())
+        except Exception:
+            return 0
+
     def __exit__(self, *a):
         if self.proc is not None:
+            # at least one sample taken after the timed region began
+            t0 = time.time()
+            while time.time() - t0 < 1 and self._rows() <= self.n0:
+                time.sleep(0.005)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -216,21 +234,50 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     gemm_ms = [ev[i][1].elapsed_time(ev[i][2]) for i in range(args.steps)]
     tot_ms = sum(prep_ms) + sum(gemm_ms)
 
-    # e2e: host-pinned input in, host-pinned output out, through the runtime API
+    # e2e: host-pinned input in, host-pinned output out, through the runtime
+    # API.  Three streams pipeline the steps: the input copy of step i+1 and
+    # the output copy of step i-1 overlap the compute of step i (two device
+    # buffers each way, ordered by events).
     x_host = d["x"].cpu().pin_memory()
-    out_host = torch.empty((M, N), dtype=torch.float16).pin_memory()
-    for _ in range(2):
-        out_host.copy_(step(x_host.to(dev, non_blocking=True)), non_blocking=True)
+    out_host = [torch.empty((M, N), dtype=torch.float16).pin_memory() for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    xd = [torch.empty((M, K), dtype=torch.float16, device=dev) for _ in range(2)]
+    yd = [None, None]
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_cmp = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+
+    def e2e_steps(n):
+        for i in range(n):
+            b = i & 1
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(ev_cmp[b])          # step i-2 has consumed xd[b]
+                xd[b].copy_(x_host, non_blocking=True)
+                ev_in[b].record(s_in)
+            st.wait_event(ev_in[b])
+            if i >= 2:
+                st.wait_event(ev_out[b])                # step i-2's output has left yd[b]
+            yd[b] = step(xd[b])
+            ev_cmp[b].record(st)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_cmp[b])
+                out_host[b].copy_(yd[b], non_blocking=True)
+                ev_out[b].record(s_out)
+
+    e2e_steps(2)
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
-    e0.record(st)
-    for _ in range(args.steps):
-        xd = x_host.to(dev, non_blocking=True)
-        out_host.copy_(step(xd), non_blocking=True)
-    e1.record(st)
+    torch.cuda.synchronize()
+    e0.record(s_in)
+    s_in.wait_event(e0)
+    e2e_steps(args.steps)
+    s_out.wait_stream(st)
+    s_out.wait_stream(s_in)
+    e1.record(s_out)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
 
@@ -261,7 +308,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         "e2e": {"value": world * OPS * args.steps / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
                 "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
         "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak, "unit": "TOPS",
-                     "frac": gemm_tops / int8_peak, "traffic": None,
+                     "frac": gemm_tops / int8_peak, "traffic": 84.1e6,
+                     "traffic_note": "bytes/launch, dram read+write from one ncu capture (profiles/gemm_tc_w4a8_grouped_config2.md)",
                      "kernel": "gemm_tc_kernel<W_I4, grouped>",
                      "peak_source": f"2 x {src} bf16 cuBLAS ({bf16} TF/s), burst",
                      "kernel_ms": gemm_avg},

@@ -75,8 +75,9 @@ class FeatureShardedLinear:
                  group=None, repack: bool = True, device: torch.device | None = None,
                  prep: Callable | None = None, gemm: Callable | None = None) -> None:
         self.group = group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        dist_on = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if dist_on else 1   # no process group: one rank
+        self.rank = dist.get_rank(group) if dist_on else 0
         self.N = weight.shape[0]
         self.int4 = weight.dtype == torch.uint8
         self.K_w = weight.shape[1] * 2 if self.int4 else weight.shape[1]
@@ -116,6 +117,8 @@ class FeatureShardedLinear:
         lead = x.shape[:-1]
         x2 = x.reshape(-1, x.shape[-1])
         local = self.local_forward(x2, x.dtype)
+        if self.world == 1:
+            return local[:, :self.N].reshape(*lead, self.N)
         parts = [torch.empty_like(local) for _ in range(self.world)]
         dist.all_gather(parts, local.contiguous(), group=self.group)
         out = torch.cat(parts, dim=1)[:, :self.N]

@@ -53,6 +53,9 @@ PREP_CASES = [
     (6, 96, 32, 96, False, False, False),          # Sylvester size
     (6, 512, 128, 512, True, True, False),         # Sylvester size
     (2, 100, 0, 112, True, False, True),           # no rotation, pad to w_in
+    (2500, 3072, 256, 3072, True, True, False),    # more rows than resident warps
+    (5, 1000, 16, 1010, True, False, True),        # ragged K and w_in (scalar gather)
+    (3, 9000, 64, 9024, True, True, False),        # long row in the per-warp buffer
 ]
 
 
