@@ -319,6 +319,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         "wall_ms": t_wall * 1e3,
         "clocks": clk.summary(),
     }
+    if world == 1 and not args.no_secondary:
+        line["secondary"] = secondary_lines(dev, flush, hbm, int8_peak, bf16)
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline()
     print(json.dumps(line), flush=True)
@@ -385,6 +387,207 @@ def run_features(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def secondary_lines(dev, flush, hbm_gbs: float, int8_peak: float, bf16_peak: float, reps: int = 20) -> dict:
+    """BASELINE configs[0] (W8A8, M=256) and configs[2] (W4A16 small M + LoRA)
+    on the GPU: median CUDA-event time per call, L2 flushed before each call
+    (outside the events), so weights come from HBM every time."""
+    import torch
+    rt = _pkg()
+    st = torch.cuda.current_stream()
+    g = torch.Generator().manual_seed(0)
+
+    def timed(fn):
+        fn()
+        ts = []
+        for i in range(reps):
+            flush.fill_(float(i))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return sorted(ts)[len(ts) // 2]
+
+    out = {}
+    # configs[0]: W8A8 linear, M=256, K=N=3072, rot 256, bias, per-channel scales
+    M1, K1 = 256, 3072
+    x = torch.randn(M1, K1, generator=g)
+    x[:, torch.randperm(K1, generator=g)[: round(0.01 * K1)]] *= 20
+    x = x.half().to(dev)
+    w8 = torch.randint(-127, 128, (K1, K1), generator=g, dtype=torch.int8).to(dev)
+    s8 = (torch.rand(K1, 1, generator=g) * 9e-3 + 1e-3).half().float().to(dev)
+    b8 = (torch.randn(K1, generator=g) * 0.02).half().to(dev)
+
+    def w8a8():
+        xq, s_a, _, _ = rt.prep_quantize(x, rot_size=256)
+        return rt.gemm_a8(xq, w8, s8, s_a, bias=b8, out_dtype=torch.float16)
+    ms = timed(w8a8)
+    byt = M1 * K1 * 2 + K1 * K1 + M1 * K1 * 2
+    out["config1_w8a8_m256"] = {"ms": ms, "tops": 2 * M1 * K1 * K1 / (ms * 1e-3) / 1e12,
+                                "gbs": byt / (ms * 1e-3) / 1e9, "hbm_frac": byt / (ms * 1e-3) / 1e9 / hbm_gbs,
+                                "kernels": 2, "note": "prep + GEMM, HBM-bound shape (12.6 MB)"}
+    # configs[2]: W4A16, rot 0, group-128 scales, rank-32 LoRA (strength 1)
+    N3 = K3 = 3072
+    q = torch.randint(-8, 8, (N3, K3), generator=g, dtype=torch.int8)
+    qu = (q.to(torch.int16) & 0xF).to(torch.uint8)
+    packed = (qu[:, 0::2] | (qu[:, 1::2] << 4)).contiguous().to(dev)
+    w1 = rt.repack_int4(packed, K3, 1)
+    sc = (torch.rand(N3, K3 // 128, generator=g) * (2e-2 - 1e-3) + 1e-3).half().to(dev)
+    down = (torch.randn(32, K3, generator=g) * 0.01).half().to(dev)
+    up = (torch.randn(N3, 32, generator=g) * 0.01).half().to(dev)
+    for M3 in (1, 16, 256):
+        x3 = torch.randn(M3, K3, generator=g).half().to(dev)
+
+        def w4a16():
+            mid = rt.lowrank_down(x3, down)
+            return rt.gemm_w4a16(x3, w1, sc, group_size=128, lr_mid=mid, lr_up=up, lr_scale=1.0, w_layout=1)
+        ms = timed(w4a16)
+        byt = N3 * K3 // 2 + sc.numel() * 2 + (down.numel() + up.numel()) * 2 + 2 * M3 * K3 * 2
+        fl = 2 * M3 * N3 * K3 + 4 * M3 * 32 * K3
+        out[f"config3_w4a16_lora_m{M3}"] = {
+            "ms": ms, "gbs": byt / (ms * 1e-3) / 1e9, "hbm_frac": byt / (ms * 1e-3) / 1e9 / hbm_gbs,
+            "tflops": fl / (ms * 1e-3) / 1e12, "bf16_frac": fl / (ms * 1e-3) / 1e12 / bf16_peak,
+            "kernels": 2, "note": "low-rank down + W4A16 with the LoRA term fused"}
+    return out
+
+
+class _QLinear:
+    """INT4 W4A8 linear with group-128 scales, SmoothRot, rot 256 and a random
+    PermuQuant perm -- the layer of BASELINE configs[3], run through the
+    runtime's fused prep and GEMM (random-init weights)."""
+
+    def __init__(self, rt, n_out: int, n_in: int, g, dev):
+        import torch
+        q = torch.randint(-8, 8, (n_out, n_in), generator=g, dtype=torch.int8)
+        qu = (q.to(torch.int16) & 0xF).to(torch.uint8)
+        self.rt = rt
+        self.w = rt.repack_int4((qu[:, 0::2] | (qu[:, 1::2] << 4)).contiguous().to(dev), n_in, 0)
+        self.s = (torch.rand(n_out, n_in // GS, generator=g) * 2e-3 + 1e-4).float().to(dev)
+        self.sr = (torch.rand(n_in, generator=g) * 3.5 + 0.5).half().float().to(dev)
+        self.perm = torch.randperm(n_in, generator=g).to(torch.int32).to(dev)
+        self.b = (torch.randn(n_out, generator=g) * 0.02).half().to(dev)
+        self.n_in = n_in
+
+    def __call__(self, x):
+        import torch
+        x2 = x.reshape(-1, x.shape[-1])
+        xq, s_a, _, _ = self.rt.prep_quantize(x2, smoothrot=self.sr, rot_size=ROT, w_in=self.n_in, perm=self.perm)
+        y = self.rt.gemm_a8(xq, self.w, self.s, s_a, bias=self.b, out_dtype=x.dtype, group_size=GS, repacked=True)
+        return y.reshape(*x.shape[:-1], y.shape[-1])
+
+
+class FluxDoubleBlock:
+    """Flux-class MMDiT double-stream block: hidden 3072,
+    24 heads x 128, MLP 12288 GELU(tanh), adaLN modulation from a 3072-d
+    vector, separate image / text weights, joint attention over text + image
+    tokens.  Every linear is the quantised layer above; norms, modulation,
+    GELU and attention (torch SDPA) run in fp16.  Random-init weights."""
+
+    def __init__(self, rt, dev, seed=0, hidden=3072, heads=24, mlp=12288):
+        import torch
+        g = torch.Generator().manual_seed(seed)
+        self.h, self.nh = hidden, heads
+        mk = lambda o, i: _QLinear(rt, o, i, g, dev)
+        self.mod = {s: mk(6 * hidden, hidden) for s in ("img", "txt")}
+        self.qkv = {s: mk(3 * hidden, hidden) for s in ("img", "txt")}
+        self.proj = {s: mk(hidden, hidden) for s in ("img", "txt")}
+        self.fc1 = {s: mk(mlp, hidden) for s in ("img", "txt")}
+        self.fc2 = {s: mk(hidden, mlp) for s in ("img", "txt")}
+        self.qn = {s: (1 + 0.1 * torch.randn(128, generator=g)).half().to(dev) for s in ("img", "txt")}
+        self.kn = {s: (1 + 0.1 * torch.randn(128, generator=g)).half().to(dev) for s in ("img", "txt")}
+
+    def linear_ops(self, n_img: int, n_txt: int) -> float:
+        h, m = self.h, self.fc1["img"].w.shape[0]
+        per_tok = 2 * h * (3 * h + h + m) + 2 * m * h
+        return (n_img + n_txt) * per_tok + 2 * 2 * (6 * h) * h
+
+    def __call__(self, img, txt, vec):
+        import torch
+        import torch.nn.functional as F
+        h, nh = self.h, self.nh
+        B = img.shape[0]
+        vs = F.silu(vec)
+        mods = {s: self.mod[s](vs).chunk(6, dim=-1) for s in ("img", "txt")}
+        qs, ks, vv = [], [], []
+        for s, x in (("txt", txt), ("img", img)):
+            sh, sc, _, _, _, _ = mods[s]
+            xn = F.layer_norm(x, (h,)) * (1 + sc[:, None]) + sh[:, None]
+            q, k, v = self.qkv[s](xn).view(B, -1, 3, nh, h // nh).permute(2, 0, 3, 1, 4)
+            q = F.rms_norm(q, (h // nh,), self.qn[s])
+            k = F.rms_norm(k, (h // nh,), self.kn[s])
+            qs.append(q); ks.append(k); vv.append(v)
+        a = F.scaled_dot_product_attention(torch.cat(qs, 2), torch.cat(ks, 2), torch.cat(vv, 2))
+        a = a.transpose(1, 2).reshape(B, -1, h)
+        nt = txt.shape[1]
+        outs = []
+        for s, x, att in (("txt", txt, a[:, :nt]), ("img", img, a[:, nt:])):
+            _, _, g1, sh2, sc2, g2 = mods[s]
+            x = x + g1[:, None] * self.proj[s](att)
+            xn = F.layer_norm(x, (h,)) * (1 + sc2[:, None]) + sh2[:, None]
+            x = x + g2[:, None] * self.fc2[s](F.gelu(self.fc1[s](xn), approximate="tanh"))
+            outs.append(x)
+        return outs[1], outs[0]
+
+
+def run_block(args, rank: int, world: int, local_rank: int) -> None:
+    """one Flux-class double block, 4096 image + 512
+    text tokens, batch 1 per GPU (token sharding across GPUs: each rank runs
+    its own sample; weights replicated; no collective).  tokens/s = 4608 x
+    ranks / max-over-ranks block time."""
+    import torch
+    import torch.distributed as dist
+    rt = _pkg()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    blk = FluxDoubleBlock(rt, dev)
+    g = torch.Generator().manual_seed(100 + rank)
+    img = torch.randn(1, 4096, 3072, generator=g).half().to(dev)
+    txt = torch.randn(1, 512, 3072, generator=g).half().to(dev)
+    vec = torch.randn(1, 3072, generator=g).half().to(dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    st = torch.cuda.current_stream()
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            blk(img, txt, vec)
+        torch.cuda.synchronize()
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        with Clocks(local_rank) as clk:
+            for i in range(args.steps):
+                flush.fill_(float(i))
+                ev[i][0].record(st)
+                blk(img, txt, vec)
+                ev[i][1].record(st)
+            torch.cuda.synchronize()
+    tot = sum(e[0].elapsed_time(e[1]) for e in ev)
+    vals = torch.tensor([tot], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    if rank != 0:
+        return
+    ms = vals.item() / args.steps
+    n_tok = 4096 + 512
+    lin = blk.linear_ops(4096, 512)
+    attn = 4 * n_tok * n_tok * 3072
+    line = {
+        "metric": "flux_double_block_tokens_per_s", "value": world * n_tok / (ms * 1e-3), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8+fp16",
+        "data": "synthetic (random-init weights)",
+        "config": {"workload": "config4 Flux double block: 4096 img + 512 txt tokens, hidden 3072, 24x128 heads, "
+                               "MLP 12288, all linears INT4 W4A8 g128 rot256 perm; attention fp16 SDPA",
+                   "parallelism": f"token-sharded x{world} (one sample per GPU, no collective)",
+                   "l2": "flushed (256 MB write) between timed steps"},
+        "linear_tops": world * lin / (ms * 1e-3) / 1e12, "attn_tflop_per_step": attn / 1e12,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def kernel_probe(which: str) -> None:
     """Three launches of one kernel of the config-2 step (for ncu captures)."""
     import torch
@@ -412,6 +615,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the configs[0] / configs[2] measurements added to the N=1 line")
+    ap.add_argument("--workload", choices=["linear", "flux_block"], default="linear",
+                    help="linear: BASELINE configs[1] (default); flux_block: configs[3]")
     ap.add_argument("--shard", choices=["tokens", "features"], default="tokens",
                     help="tokens: every rank runs its own 4096 tokens (default); "
                          "features: one layer split by output features + all-gather")
@@ -434,7 +641,10 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120))
     try:
-        (run_features if args.shard == "features" else run_gpu)(args, rank, world, local_rank)
+        if args.workload == "flux_block":
+            run_block(args, rank, world, local_rank)
+        else:
+            (run_features if args.shard == "features" else run_gpu)(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -197,12 +197,18 @@ def gemm_a8(
     rowsum: torch.Tensor | None = None,
     zp_corr: torch.Tensor | None = None,
     repacked: bool = False,
+    splits: int | None = None,
 ) -> torch.Tensor:
     """``out = s_a[m] * sum_g s_w[n,g] * (xq @ w^T)_g + bias - rowsum (x) zp_corr``.
 
     ``w`` is int8 ``[N, K]`` or packed INT4 uint8 ``[N, K/2]``; ``s_w`` is
     ``[N]``/``[N,1]`` (per channel) or ``[N, G]`` (groups of ``group_size``,
     default ``ceil(K / G)`` rounded to a multiple of 128).
+
+    ``splits`` cuts K into that many parts run as separate work units (split-K,
+    fp32 partials in a workspace allocated here, then a reduce kernel); None
+    picks it from the tile count so that small-M calls fill the GPU
+    (``INTCRUSH_SPLITK=0`` turns that off).
     """
     _need_cuda("gemm_a8", x_int8, w, s_w, s_a, bias, out, rowsum, zp_corr)
     if x_int8.dtype != torch.int8:
@@ -240,12 +246,60 @@ def gemm_a8(
     b = None if bias is None else bias.contiguous()
     rs = _f32c(rowsum)
     zc = _f32c(zp_corr)
+    if splits is None:
+        splits = _auto_splits(M, N, K, G, gs, x_int8.device, kind != L.IC_W_INT8)
+    if splits > 1:
+        ws = torch.empty(splits * M * N, dtype=torch.float32, device=x_int8.device)
+        st = L.lib().ic_gemm_a8_splitk(
+            _p(x_int8), M, K, x_int8.stride(0), _p(w), kind, N, w.stride(0), _p(sw), G, gs, _p(sa),
+            _p(b), _DT[b.dtype] if b is not None else 0, _p(rs), _p(zc), _p(out), _DT[out.dtype], out.stride(0),
+            int(splits), _p(ws), ws.numel(), _stream(x_int8))
+        L.check(st, "ic_gemm_a8_splitk")
+        return out
     st = L.lib().ic_gemm_a8(
         _p(x_int8), M, K, x_int8.stride(0), _p(w), kind, N, w.stride(0), _p(sw), G, gs, _p(sa),
         _p(b), _DT[b.dtype] if b is not None else 0, _p(rs), _p(zc), _p(out), _DT[out.dtype], out.stride(0),
         _stream(x_int8))
     L.check(st, "ic_gemm_a8")
     return out
+
+
+_SMS: dict = {}
+
+
+def _num_sms(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SMS:
+        _SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SMS[idx]
+
+
+def _auto_splits(M: int, N: int, K: int, G: int, gs: int, device: torch.device, int4: bool) -> int:
+    """Split-K factor for ``gemm_a8``: 1 unless the output tiles cover less
+    than half of the SMs; then the largest divisor of the K-block count (and
+    of G for group scales) that keeps at least 4 K blocks per part and the
+    work units within one wave."""
+    if os.environ.get("INTCRUSH_SPLITK", "1") == "0":
+        return 1
+    grouped = G > 1
+    # token-tile width as the library picks it (pick_bn in gemm_tc.cu)
+    sms = _num_sms(device)
+    bn = 32 if M <= 32 else 64 if M <= 64 else 128 if M <= 128 else (192 if grouped else 256)
+    while bn > 64 and -(-M // bn) * -(-N // 128) * 2 < sms:
+        bn = 128 if bn > 128 else 64
+    tiles = -(-M // bn) * -(-N // 128)
+    if tiles * 2 > sms:
+        return 1
+    nkb = -(-K // 128)
+    best = 1
+    for d in range(2, 17):
+        if nkb % d or nkb // d < 4:
+            continue
+        if grouped and (K % gs or G % d):
+            continue
+        if tiles * d <= sms:
+            best = d
+    return best
 
 
 def fused_int8_gemm_dequant(

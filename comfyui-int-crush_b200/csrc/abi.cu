@@ -105,42 +105,70 @@ int ic_dynamic_quantize(const void* x, int x_dtype, int64_t M, int64_t K, int64_
                        nullptr, stream);
 }
 
-int ic_gemm_a8(const int8_t* xq, int64_t M, int64_t K, int64_t ldq, const void* w, int w_kind, int64_t N,
+static int gemm_a8_impl(const char* fn, const int8_t* xq, int64_t M, int64_t K, int64_t ldq, const void* w, int w_kind, int64_t N,
                int64_t ldw, const float* s_w, int64_t G, int64_t group_size, const float* s_a,
                const void* bias, int bias_dtype, const float* rowsum, const float* zp_corr, void* out,
-               int out_dtype, int64_t ldo, void* stream) {
+               int out_dtype, int64_t ldo, int splits, float* ws, int64_t ws_elems,
+                        void* stream) {
   g_err[0] = 0;
-  if (M < 0 || N < 0 || K <= 0) return fail(IC_ERR_ARG, "ic_gemm_a8: bad M/N/K");
+  if (M < 0 || N < 0 || K <= 0) return fail(IC_ERR_ARG, "%s: bad M/N/K", fn);
   if (M == 0 || N == 0) return IC_OK;
-  if (!xq || !w || !s_w || !s_a || !out) return fail(IC_ERR_ARG, "ic_gemm_a8: NULL operand");
-  if (w_kind != IC_W_INT8 && w_kind != IC_W_INT4 && w_kind != IC_W_INT4R) return fail(IC_ERR_ARG, "ic_gemm_a8: bad w_kind");
-  if (out_dtype < IC_DTYPE_F16 || out_dtype > IC_DTYPE_F32) return fail(IC_ERR_ARG, "ic_gemm_a8: bad out dtype");
-  if (bias && (bias_dtype < IC_DTYPE_F16 || bias_dtype > IC_DTYPE_F32)) return fail(IC_ERR_ARG, "ic_gemm_a8: bad bias dtype");
-  if ((rowsum == nullptr) != (zp_corr == nullptr)) return fail(IC_ERR_ARG, "ic_gemm_a8: rowsum and zp_corr go together");
-  if (ldq < K || ldq % 16 || !aligned16(xq)) return fail(IC_ERR_ARG, "ic_gemm_a8: xq needs ldq >= K, ldq %% 16 == 0, 16-byte alignment");
-  if (!aligned16(w) || ldw % 16) return fail(IC_ERR_ARG, "ic_gemm_a8: weights need 16-byte aligned base and row stride");
-  if (w_kind == IC_W_INT8 && (K % 16 || ldw < K)) return fail(IC_ERR_ARG, "ic_gemm_a8: int8 weights need K %% 16 == 0 and ldw >= K");
-  if (w_kind != IC_W_INT8 && (K % 32 || ldw < K / 2)) return fail(IC_ERR_ARG, "ic_gemm_a8: int4 weights need K %% 32 == 0 and ldw >= K/2");
-  if (ldo < N) return fail(IC_ERR_ARG, "ic_gemm_a8: ldo < N");
-  if (G < 1) return fail(IC_ERR_ARG, "ic_gemm_a8: G must be >= 1");
+  if (!xq || !w || !s_w || !s_a || !out) return fail(IC_ERR_ARG, "%s: NULL operand", fn);
+  if (w_kind != IC_W_INT8 && w_kind != IC_W_INT4 && w_kind != IC_W_INT4R) return fail(IC_ERR_ARG, "%s: bad w_kind", fn);
+  if (out_dtype < IC_DTYPE_F16 || out_dtype > IC_DTYPE_F32) return fail(IC_ERR_ARG, "%s: bad out dtype", fn);
+  if (bias && (bias_dtype < IC_DTYPE_F16 || bias_dtype > IC_DTYPE_F32)) return fail(IC_ERR_ARG, "%s: bad bias dtype", fn);
+  if ((rowsum == nullptr) != (zp_corr == nullptr)) return fail(IC_ERR_ARG, "%s: rowsum and zp_corr go together", fn);
+  if (ldq < K || ldq % 16 || !aligned16(xq)) return fail(IC_ERR_ARG, "%s: xq needs ldq >= K, ldq %% 16 == 0, 16-byte alignment", fn);
+  if (!aligned16(w) || ldw % 16) return fail(IC_ERR_ARG, "%s: weights need 16-byte aligned base and row stride", fn);
+  if (w_kind == IC_W_INT8 && (K % 16 || ldw < K)) return fail(IC_ERR_ARG, "%s: int8 weights need K %% 16 == 0 and ldw >= K", fn);
+  if (w_kind != IC_W_INT8 && (K % 32 || ldw < K / 2)) return fail(IC_ERR_ARG, "%s: int4 weights need K %% 32 == 0 and ldw >= K/2", fn);
+  if (ldo < N) return fail(IC_ERR_ARG, "%s: ldo < N", fn);
+  if (G < 1) return fail(IC_ERR_ARG, "%s: G must be >= 1", fn);
   if (G > 1) {
-    if (group_size <= 0 || group_size % 128) return fail(IC_ERR_UNSUPPORTED, "ic_gemm_a8: group_size must be a multiple of 128");
-    if ((K + group_size - 1) / group_size != G) return fail(IC_ERR_ARG, "ic_gemm_a8: G != ceil(K / group_size)");
+    if (group_size <= 0 || group_size % 128) return fail(IC_ERR_UNSUPPORTED, "%s: group_size must be a multiple of 128", fn);
+    if ((K + group_size - 1) / group_size != G) return fail(IC_ERR_ARG, "%s: G != ceil(K / group_size)", fn);
     if (w_kind == IC_W_INT8 && group_size > 128)
-      return fail(IC_ERR_UNSUPPORTED, "ic_gemm_a8: int8 weights with group scales need group_size == 128");
+      return fail(IC_ERR_UNSUPPORTED, "%s: int8 weights with group scales need group_size == 128", fn);
   }
-  if (M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL) return fail(IC_ERR_UNSUPPORTED, "ic_gemm_a8: dims >= 2^31");
+  if (M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL) return fail(IC_ERR_UNSUPPORTED, "%s: dims >= 2^31", fn);
   ic::GemmArgs a;
   memset(&a, 0, sizeof(a));
   a.G = (int)G; a.kb_per_group = G > 1 ? (int)(group_size / 128) : 0; a.group_size = (int)group_size;
   a.s_w = s_w; a.s_a = s_a; a.bias = bias; a.bias_dtype = bias_dtype; a.rowsum = rowsum; a.zp_corr = zp_corr;
   a.out = out; a.out_dtype = out_dtype; a.ldo = ldo;
   a.w_repacked = (w_kind == IC_W_INT4R);
+  if (splits < 1 || splits > 16) return fail(IC_ERR_ARG, "%s: splits must be in [1, 16]", fn);
+  if (splits > 1) {
+    const int64_t nkb = (K + 127) / 128;
+    if (nkb % splits) return fail(IC_ERR_ARG, "%s: ceil(K / 128) must be a multiple of splits", fn);
+    if (G > 1 && (K % group_size || G % splits))
+      return fail(IC_ERR_ARG, "%s: with group scales, K %% group_size == 0 and G %% splits == 0", fn);
+    if (!ws || ws_elems < (int64_t)splits * M * N) return fail(IC_ERR_ARG, "%s: workspace needs splits*M*N floats", fn);
+  }
+  a.splits = splits;
+  a.ws = ws;
   const char* why = "kernel launch";
   const int force_bn = 0;
   cudaError_t e = ic::launch_gemm_a8(xq, (int)M, (int)K, ldq, w, w_kind == IC_W_INT8 ? IC_W_INT8 : IC_W_INT4, (int)N, ldw, a, force_bn,
                                      (cudaStream_t)stream, &why);
   return cuda_status(e, why);
+}
+
+int ic_gemm_a8(const int8_t* xq, int64_t M, int64_t K, int64_t ldq, const void* w, int w_kind, int64_t N,
+               int64_t ldw, const float* s_w, int64_t G, int64_t group_size, const float* s_a,
+               const void* bias, int bias_dtype, const float* rowsum, const float* zp_corr, void* out,
+               int out_dtype, int64_t ldo, void* stream) {
+  return gemm_a8_impl("ic_gemm_a8", xq, M, K, ldq, w, w_kind, N, ldw, s_w, G, group_size, s_a, bias, bias_dtype,
+                      rowsum, zp_corr, out, out_dtype, ldo, 1, nullptr, 0, stream);
+}
+
+int ic_gemm_a8_splitk(const int8_t* xq, int64_t M, int64_t K, int64_t ldq, const void* w, int w_kind, int64_t N,
+                      int64_t ldw, const float* s_w, int64_t G, int64_t group_size, const float* s_a,
+                      const void* bias, int bias_dtype, const float* rowsum, const float* zp_corr, void* out,
+                      int out_dtype, int64_t ldo, int splits, float* workspace, int64_t workspace_elems,
+                      void* stream) {
+  return gemm_a8_impl("ic_gemm_a8_splitk", xq, M, K, ldq, w, w_kind, N, ldw, s_w, G, group_size, s_a, bias,
+                      bias_dtype, rowsum, zp_corr, out, out_dtype, ldo, splits, workspace, workspace_elems, stream);
 }
 
 int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const uint8_t* w, int64_t N,

@@ -63,6 +63,13 @@ struct GemmArgs {
   void* out;
   int out_dtype;
   long long ldo;
+  // split-K: each (tile, split) work unit covers kb_per_unit consecutive K
+  // blocks; with splits > 1 the epilogue stores fp32 partials (scaled by s_a
+  // and s_w, without bias or zero-point term) to ws [splits, M, N] and
+  // splitk_reduce_kernel finishes the output
+  int splits;
+  int kb_per_unit;
+  float* ws;
 };
 
 constexpr int kTileN = 128;            // weight rows per tile (UMMA M)
@@ -212,6 +219,36 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, const float* v, i
     store_chunk_t(a, reinterpret_cast<float*>(a.out), v, m0, n, nvalid, bias_n, zpc_n, lane);
 }
 
+// Split-K partial of 32 consecutive tokens of feature n:
+// ws[split, m, n] = v[j] * s_a[m] (fp32; bias and zero point come in the reduce).
+__device__ __forceinline__ void store_partial(const GemmArgs& a, const float* v, int split, int m0, int n,
+                                              bool nvalid, int lane) {
+  const int ml = m0 + lane;
+  const float sa_b = (ml < a.M) ? __ldg(&a.s_a[ml]) : 0.f;
+  const int jmax = nvalid ? min(32, a.M - m0) : 0;
+  float* p = a.ws + ((size_t)split * a.M + m0) * a.N + n;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float sa = __shfl_sync(0xffffffffu, sa_b, j);
+    if (j < jmax) *p = v[j] * sa;
+    p += a.N;
+  }
+}
+
+// out[m, n] = sum_s ws[s, m, n] + bias[n] - rowsum[m] * zp_corr[n]
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmArgs a) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long MN = (long long)a.M * a.N;
+  if (i >= MN) return;
+  const int m = (int)(i / a.N), n = (int)(i % a.N);
+  float v = 0.f;
+  for (int s = 0; s < a.splits; ++s) v += a.ws[(long long)s * MN + i];
+  const float bias_n = a.bias ? load_any(a.bias, a.bias_dtype, n) : 0.f;
+  const float rs = a.rowsum ? a.rowsum[m] : 0.f;
+  const float zc = a.zp_corr ? a.zp_corr[n] : 0.f;
+  store_out(a.out, a.out_dtype, (size_t)m * a.ldo + n, fmaf(-rs, zc, v + bias_n));
+}
+
 // W4A16: out[m, n] = fp16(v[j] + bias_n) (no activation scale).
 __device__ __forceinline__ void store_chunk_raw(const GemmArgs& a, const float* v, int m0, int n, bool nvalid,
                                                 float bias_n) {
@@ -303,8 +340,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int total_tiles = a.m_tiles * a.n_tiles;
-  const int units = GROUPED ? a.G : 1;
+  const int total_units = a.m_tiles * a.n_tiles * a.splits;
+  // accumulation units (one K group each when GROUPED) per work unit
+  const int units = GROUPED ? a.kb_per_unit / a.kb_per_group : 1;
 
   auto x_stage = [&](int s) { return smem + C::OFF_X + s * C::XSTAGE + (C::I4 ? 0 : C::W_BYTES); };
   auto w_stage = [&](int s) {
@@ -317,9 +355,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+      for (int wu = blockIdx.x; ok && wu < total_units; wu += gridDim.x) {
+        const int tile = wu / a.splits, kb_lo = (wu % a.splits) * a.kb_per_unit;
         const int n_blk = tile / a.m_tiles, m_blk = tile % a.m_tiles;
-        for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
+        for (int kb = kb_lo; kb < kb_lo + a.kb_per_unit; ++kb, ++it) {
           const int s = it % SX;
           const uint32_t ph = (uint32_t)(it / SX) & 1u;
           { IC_T0();
@@ -349,10 +388,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       const uint64_t magic_b = smem_desc_sw128(smem_u32(smem + 1024)) & ~(0x3FFFull << 32);
       int it = 0, uc = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+      for (int wu = blockIdx.x; ok && wu < total_units; wu += gridDim.x) {
+        const int kb_lo = (wu % a.splits) * a.kb_per_unit;
         for (int u = 0; ok && u < units; ++u, ++uc) {
-          const int kb0 = GROUPED ? u * a.kb_per_group : 0;
-          const int kb1 = GROUPED ? min(kb0 + a.kb_per_group, a.num_kb) : a.num_kb;
+          const int kb0 = GROUPED ? kb_lo + u * a.kb_per_group : kb_lo;
+          const int kb1 = GROUPED ? min(kb0 + a.kb_per_group, kb_lo + a.kb_per_unit) : kb_lo + a.kb_per_unit;
           const int b = uc % NB;
           { IC_T0();
           if (!mbar_wait(&acc_empty[b], (uint32_t)(uc / NB) & 1u, abort_flag)) { ok = false; break; }
@@ -402,10 +442,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       const int xw = warp - 2;
       int issued = 0;
       auto issue_p = [&](int j) {
-        const int tile_j = blockIdx.x + (j / a.num_kb) * gridDim.x;
-        if (tile_j >= total_tiles) return;
-        const int kb = j % a.num_kb;
-        const int n_blk = tile_j / a.m_tiles;
+        const int wu_j = blockIdx.x + (j / a.kb_per_unit) * gridDim.x;
+        if (wu_j >= total_units) return;
+        const int kb = (wu_j % a.splits) * a.kb_per_unit + j % a.kb_per_unit;
+        const int n_blk = (wu_j / a.splits) / a.m_tiles;
         const int sp = j % SP;
         mbar_arrive_expect_tx(&p_full[sp], (uint32_t)C::P_BYTES);
         tma_load_2d(p_stage(sp), &tm_w, &p_full[sp], kb * (MODE == W_I4 ? 64 : 32), n_blk * kTileN);
@@ -416,9 +456,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       int it = 0;
       bool ok = true;
       const bool rp = a.w_repacked != 0;
-      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
-        const int n_blk = tile / a.m_tiles;
-        for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
+      for (int wu = blockIdx.x; ok && wu < total_units; wu += gridDim.x) {
+        const int n_blk = (wu / a.splits) / a.m_tiles, kb_lo = (wu % a.splits) * a.kb_per_unit;
+        for (int kb = kb_lo; kb < kb_lo + a.kb_per_unit; ++kb, ++it) {
           if ((it & 1) != xw) continue;
           const int sp = it % SP, sw = it % SW;
           IC_T0();
@@ -550,7 +590,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       for (int b = 0; b < NB; ++b) mbar_arrive(&acc_empty[b]);
     int uc = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+    for (int wu = blockIdx.x; ok && wu < total_units; wu += gridDim.x) {
+      const int tile = wu / a.splits, split = wu % a.splits;
       const int n_blk = tile / a.m_tiles, m_blk = tile % a.m_tiles;
       const int n = n_blk * kTileN + 32 * q + lane;
       const bool nvalid = n < a.N;
@@ -562,7 +603,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
 #pragma unroll
         for (int j = 0; j < C::CPT / 2; ++j) accp[j] = 0ull;
         const unsigned long long mg2 = pack2(-kMagicF, -kMagicF);
-        const float* swrow = a.s_w + (size_t)(nvalid ? n : 0) * a.G;
+        const float* swrow = a.s_w + (size_t)(nvalid ? n : 0) * a.G + (size_t)split * units;
         float sw = nvalid ? __ldg(swrow) * wmul : 0.f;
         for (int u = 0; u < units; ++u, ++uc) {
           const int b = uc % NB;
@@ -603,7 +644,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
             v[2 * j] = __uint_as_float((uint32_t)accp[16 * c + j]);
             v[2 * j + 1] = __uint_as_float((uint32_t)(accp[16 * c + j] >> 32));
           }
-          store_chunk(a, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane);
+          if (a.splits > 1) store_partial(a, v, split, mbase + 32 * c, n, nvalid, lane);
+          else store_chunk(a, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane);
         }
       } else {
         const int b = uc % NB;
@@ -621,6 +663,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           for (int j = 0; j < 32; ++j)
             v[j] = (MODE == W_I4F) ? __uint_as_float(r[j]) : (float)(int)r[j] * sw;
           if constexpr (MODE == W_I4F) store_chunk_raw(a, v, mbase + 32 * c, n, nvalid, bias_n);
+          else if (a.splits > 1) store_partial(a, v, split, mbase + 32 * c, n, nvalid, lane);
           else store_chunk(a, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane);
         }
         tc_fence_before();
@@ -695,7 +738,7 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tw, const CUtensorMap& tx, c
   auto kern = gemm_tc_kernel<MODE, BN, GROUPED>;
   cudaError_t e = set_smem_once(kern, C::SMEM);
   if (e != cudaSuccess) return e;
-  const int tiles = a.m_tiles * a.n_tiles;
+  const int tiles = a.m_tiles * a.n_tiles * a.splits;   // work units
   const int grid = tiles < num_sms() ? tiles : num_sms();
   kern<<<grid, C::THREADS, C::SMEM, st>>>(tw, tx, a);
   return cudaGetLastError();
@@ -712,13 +755,16 @@ static int forced_bn() {
   return v;
 }
 
-static int pick_bn(int M, bool grouped) {
+// Widest tile for M, narrowed (down to 64 tokens) while the output tiles
+// would cover less than half of the SMs: for small problems parallelism
+// matters more than the per-instruction efficiency of wide MMAs.
+static int pick_bn(int M, int N, bool grouped) {
   const int f = forced_bn();
   if (f) return f;
-  if (M <= 32) return 32;
-  if (M <= 64) return 64;
-  if (M <= 128) return 128;
-  return grouped ? 192 : 256;
+  int bn = M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : (grouped ? 192 : 256);
+  const int n_tiles = (N + kTileN - 1) / kTileN;
+  while (bn > 64 && ((M + bn - 1) / bn) * n_tiles * 2 < num_sms()) bn = (bn > 128) ? 128 : 64;
+  return bn;
 }
 
 template <int MODE, bool GROUPED>
@@ -743,7 +789,7 @@ cudaError_t launch_gemm_a8(const int8_t* xq, int M, int K, long long ldq, const 
                            const char** why) {
   CUtensorMap tx, tw;
   const bool grouped = a.G > 1;
-  const int bn = force_bn ? force_bn : pick_bn(M, grouped);
+  const int bn = force_bn ? force_bn : pick_bn(M, N, grouped);
   if (!make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, (uint64_t)K, (uint64_t)M, (uint64_t)ldq, 128,
                  (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B)) {
     *why = "cuTensorMapEncodeTiled failed for the activation operand";
@@ -763,17 +809,24 @@ cudaError_t launch_gemm_a8(const int8_t* xq, int M, int K, long long ldq, const 
   a.M = M; a.N = N; a.K = K;
   a.num_kb = (K + 127) / 128;
   a.n_tiles = (N + kTileN - 1) / kTileN;
-  if (w_kind == IC_W_INT8) {
-    return grouped ? dispatch_bn<W_I8, true>(bn, tw, tx, a, st) : dispatch_bn<W_I8, false>(bn, tw, tx, a, st);
-  }
-  return grouped ? dispatch_bn<W_I4, true>(bn, tw, tx, a, st) : dispatch_bn<W_I4, false>(bn, tw, tx, a, st);
+  if (a.splits < 1) a.splits = 1;
+  a.kb_per_unit = a.num_kb / a.splits;
+  cudaError_t e;
+  if (w_kind == IC_W_INT8)
+    e = grouped ? dispatch_bn<W_I8, true>(bn, tw, tx, a, st) : dispatch_bn<W_I8, false>(bn, tw, tx, a, st);
+  else
+    e = grouped ? dispatch_bn<W_I4, true>(bn, tw, tx, a, st) : dispatch_bn<W_I4, false>(bn, tw, tx, a, st);
+  if (e != cudaSuccess || a.splits == 1) return e;
+  const long long mn = (long long)M * N;
+  splitk_reduce_kernel<<<(unsigned)((mn + 255) / 256), 256, 0, st>>>(a);
+  return cudaGetLastError();
 }
 
 // Entry used by ic_gemm_w4a16 for M above the skinny-kernel range.
 cudaError_t launch_gemm_w4a16_tc(const void* x, int M, int K, long long ldx, const uint8_t* w, int N,
                                  long long ldw, GemmArgs a, int force_bn, cudaStream_t st, const char** why) {
   CUtensorMap tx, tw;
-  const int bn = force_bn ? force_bn : pick_bn(M, false);
+  const int bn = force_bn ? force_bn : pick_bn(M, N, false);
   if (!make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)ldx * 2, 64,
                  (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B)) {
     *why = "cuTensorMapEncodeTiled failed for the activation operand";
@@ -787,6 +840,8 @@ cudaError_t launch_gemm_w4a16_tc(const void* x, int M, int K, long long ldx, con
   a.M = M; a.N = N; a.K = K;
   a.num_kb = (K + 63) / 64;
   a.n_tiles = (N + kTileN - 1) / kTileN;
+  a.splits = 1;
+  a.kb_per_unit = a.num_kb;
   return dispatch_bn<W_I4F, false>(bn, tw, tx, a, st);
 }
 

@@ -45,7 +45,7 @@ struct PrepArgs {
   int vec_ok;       // 16-byte vector loads of x are legal
 };
 
-constexpr int kPrepThreads = 256;
+int num_sms();   // gemm_tc.cu
 
 // Elements of a row rotated per block-wide step (a multiple of the rotation
 // size); small enough that several rows fit in one SM's shared memory.
@@ -125,8 +125,13 @@ __device__ __forceinline__ void load16(const PrepArgs& a, const T* xrow, int64_t
       if (a.smoothrot) {
         const float s0 = DT<T>::to_f(DT<T>::from_f(a.smoothrot[k0 + j]));
         const float s1 = DT<T>::to_f(DT<T>::from_f(a.smoothrot[k0 + 8 + j]));
+#if defined(IC_DIAG_NODIV)   // tuning-only timing variants (wrong results)
+        f0 = DT<T>::to_f(DT<T>::from_f(f0 * s0));
+        f1 = DT<T>::to_f(DT<T>::from_f(f1 * s1));
+#else
         f0 = DT<T>::to_f(DT<T>::from_f(__fdiv_rn(f0, s0)));
         f1 = DT<T>::to_f(DT<T>::from_f(__fdiv_rn(f1, s1)));
+#endif
       }
       v[j] = to_rot<V, T>(f0);
       v[8 + j] = to_rot<V, T>(f1);
@@ -137,7 +142,8 @@ __device__ __forceinline__ void load16(const PrepArgs& a, const T* xrow, int64_t
   }
 }
 
-// Block-wide reductions over kPrepThreads threads.
+// Block-wide reductions over NT threads.
+template <int NT>
 __device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -147,9 +153,10 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   __syncthreads();
   float r = red[0];
 #pragma unroll
-  for (int i = 1; i < kPrepThreads / 32; ++i) r = fmaxf(r, red[i]);
+  for (int i = 1; i < NT / 32; ++i) r = fmaxf(r, red[i]);
   return r;
 }
+template <int NT>
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -159,13 +166,13 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   __syncthreads();
   float r = 0.f;
 #pragma unroll
-  for (int i = 0; i < kPrepThreads / 32; ++i) r += red[i];
+  for (int i = 0; i < NT / 32; ++i) r += red[i];
   return r;
 }
 
 // One rotation pass over a chunk [c0, c0 + CH) of the row.  The pass covers
 // index bits [S, S + L) of each rotation group of size 2^LOG2R.
-template <typename T, int LOG2R, bool SYL, int S, int L, bool FIRST, bool LAST>
+template <typename T, int LOG2R, bool SYL, int S, int L, bool FIRST, bool LAST, int NT>
 __device__ __forceinline__ void rot_pass(const PrepArgs& a, const T* xrow, int c0, int CH,
                                          typename RotT<T>::V* buf, T* xr) {
   using V = typename RotT<T>::V;
@@ -173,7 +180,7 @@ __device__ __forceinline__ void rot_pass(const PrepArgs& a, const T* xrow, int c
   constexpr int E = 1 << L;
   constexpr int HIGH = R >> (S + L);
   const int items = CH >> L;
-  for (int it = threadIdx.x; it < items; it += kPrepThreads) {
+  for (int it = threadIdx.x; it < items; it += NT) {
     const int low = it & ((1 << S) - 1);
     const int rest = it >> S;
     const int high = rest % HIGH;
@@ -197,8 +204,12 @@ __device__ __forceinline__ void rot_pass(const PrepArgs& a, const T* xrow, int c
 #pragma unroll
       for (int j = 0; j < E; ++j) {
         T out;
+#if defined(IC_DIAG_NOD2H)
+        out = DT<T>::from_f((float)(v[j] * (1.0 / (double)(1 << (LOG2R / 2)))));
+#else
         if constexpr (SYL) out = DT<T>::from_d(v[j] * a.syl_h);
         else out = DT<T>::from_d(v[j] * (1.0 / (double)(1 << (LOG2R / 2))));   // 2^-D, exact
+#endif
         xr[c0 + base + (j << S)] = out;
       }
     } else {
@@ -208,7 +219,7 @@ __device__ __forceinline__ void rot_pass(const PrepArgs& a, const T* xrow, int c
   }
 }
 
-template <typename T, int LOG2R, bool SYL, int S>
+template <typename T, int LOG2R, bool SYL, int S, int NT>
 __device__ __forceinline__ void rot_passes(const PrepArgs& a, const T* xrow, int c0, int CH,
                                            typename RotT<T>::V* buf, T* xr) {
   // bits per pass: 4 (two radix-4 digits / four radix-2 stages); the last
@@ -217,17 +228,17 @@ __device__ __forceinline__ void rot_passes(const PrepArgs& a, const T* xrow, int
   constexpr int L = REM >= 4 ? 4 : REM;
   constexpr bool FIRST = (S == 0);
   constexpr bool LAST = (S + L == LOG2R);
-  rot_pass<T, LOG2R, SYL, S, L, FIRST, LAST>(a, xrow, c0, CH, buf, xr);
+  rot_pass<T, LOG2R, SYL, S, L, FIRST, LAST, NT>(a, xrow, c0, CH, buf, xr);
   if constexpr (!LAST) {
     __syncthreads();
-    rot_passes<T, LOG2R, SYL, S + L>(a, xrow, c0, CH, buf, xr);
+    rot_passes<T, LOG2R, SYL, S + L, NT>(a, xrow, c0, CH, buf, xr);
   }
 }
 
-template <typename T, int LOG2R, bool SYL>
-__global__ void __launch_bounds__(kPrepThreads) prep_quant_kernel(const PrepArgs a) {
+template <typename T, int LOG2R, bool SYL, int NT>
+__global__ void __launch_bounds__(NT) prep_quant_kernel(const PrepArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ float red[kPrepThreads / 32];
+  __shared__ float red[NT / 32];
   const int64_t row = blockIdx.x;
   const T* xrow = reinterpret_cast<const T*>(a.x) + row * a.ldx;
 
@@ -242,7 +253,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_quant_kernel(const PrepArgs
 
   // 1. load (+SmoothRot) and rotate into xr[0, Kr)
   if constexpr (LOG2R == 0) {
-    for (int k0 = threadIdx.x * 8; k0 < (int)a.K; k0 += kPrepThreads * 8) {
+    for (int k0 = threadIdx.x * 8; k0 < (int)a.K; k0 += NT * 8) {
       if (a.vec_ok && k0 + 8 <= a.K && !a.smoothrot) {
         *reinterpret_cast<uint4*>(xr + k0) = __ldg(reinterpret_cast<const uint4*>(xrow + k0));
       } else {
@@ -255,12 +266,12 @@ __global__ void __launch_bounds__(kPrepThreads) prep_quant_kernel(const PrepArgs
     const int Kr = (int)a.Kr;
     for (int c0 = 0; c0 < Kr; c0 += CH) {
       const int ch = (Kr - c0) < CH ? (Kr - c0) : CH;   // multiple of the rotation size
-      rot_passes<T, LOG2R, SYL, 0>(a, xrow, c0, ch, buf, xr);
+      rot_passes<T, LOG2R, SYL, 0, NT>(a, xrow, c0, ch, buf, xr);
       __syncthreads();
     }
   }
   // zero padding [Kr, Wp)
-  for (int k = (int)a.Kr + threadIdx.x; k < Wp; k += kPrepThreads) xr[k] = DT<T>::from_f(0.f);
+  for (int k = (int)a.Kr + threadIdx.x; k < Wp; k += NT) xr[k] = DT<T>::from_f(0.f);
   __syncthreads();
 
   // 2. gather + SmoothQuant divide into xp, row absmax (and sum).  Four
@@ -279,7 +290,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_quant_kernel(const PrepArgs
   };
   if (vec4) {
 #pragma unroll 4
-    for (int j0 = threadIdx.x * 4; j0 < w_in; j0 += kPrepThreads * 4) {
+    for (int j0 = threadIdx.x * 4; j0 < w_in; j0 += NT * 4) {
       int4 src = make_int4(j0, j0 + 1, j0 + 2, j0 + 3);
       if (a.perm) src = __ldg(reinterpret_cast<const int4*>(a.perm + j0));
       float4 sm = make_float4(1.f, 1.f, 1.f, 1.f);
@@ -292,12 +303,12 @@ __global__ void __launch_bounds__(kPrepThreads) prep_quant_kernel(const PrepArgs
       one(j0 + 3, src.w, f3);
     }
   } else {
-    for (int j = threadIdx.x; j < w_in; j += kPrepThreads)
+    for (int j = threadIdx.x; j < w_in; j += NT)
       one(j, a.perm ? a.perm[j] : j, a.smooth ? DT<T>::to_f(DT<T>::from_f(a.smooth[j])) : 1.f);
   }
-  amax = block_max(amax, red);
+  amax = block_max<NT>(amax, red);
   if (a.rowsum) {
-    const float s = block_sum(rsum, red);
+    const float s = block_sum<NT>(rsum, red);
     if (threadIdx.x == 0) a.rowsum[row] = s;
   }
   __syncthreads();   // xp complete
@@ -307,10 +318,10 @@ __global__ void __launch_bounds__(kPrepThreads) prep_quant_kernel(const PrepArgs
     T* dst = reinterpret_cast<T*>(a.x_prep) + row * (int64_t)w_in;
     const bool vec = ((w_in & 7) == 0) && ((reinterpret_cast<uintptr_t>(a.x_prep) & 15) == 0);
     if (vec) {
-      for (int j = threadIdx.x * 8; j < w_in; j += kPrepThreads * 8)
+      for (int j = threadIdx.x * 8; j < w_in; j += NT * 8)
         *reinterpret_cast<uint4*>(dst + j) = *reinterpret_cast<const uint4*>(xp + j);
     } else {
-      for (int j = threadIdx.x; j < w_in; j += kPrepThreads) dst[j] = xp[j];
+      for (int j = threadIdx.x; j < w_in; j += NT) dst[j] = xp[j];
     }
   }
 
@@ -321,7 +332,7 @@ __global__ void __launch_bounds__(kPrepThreads) prep_quant_kernel(const PrepArgs
     if (threadIdx.x == 0) a.s_a[row] = s;
     int8_t* qrow = a.xq + row * a.ldq;
     const int ldq = (int)a.ldq;
-    for (int j0 = threadIdx.x * 16; j0 < ldq; j0 += kPrepThreads * 16) {
+    for (int j0 = threadIdx.x * 16; j0 < ldq; j0 += NT * 16) {
       uint32_t wv[4];
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
@@ -340,7 +351,9 @@ __global__ void __launch_bounds__(kPrepThreads) prep_quant_kernel(const PrepArgs
             const float xv = DT<T>::to_f(xp[j]);
             float y = xv * rs;
             const float fy = fabsf(y);
+#if !defined(IC_DIAG_NOQCHK)
             if (fabsf(fy - (floorf(fy) + 0.5f)) <= fy * 4.8e-7f) y = __fdiv_rn(xv, s);
+#endif
             q = max(-128, min(127, __float_as_int(y + 12582912.0f) - 0x4B400000));
           }
           word |= ((uint32_t)(q & 0xFF)) << (8 * b);
@@ -359,13 +372,16 @@ static cudaError_t launch_prep_t(const PrepArgs& a, cudaStream_t st) {
   const bool need_xp = (a.perm != nullptr) || (a.smooth != nullptr);
   const size_t xr_elems = (size_t)((a.Wp + 7) & ~7LL);
   const size_t smem = buf_bytes + (xr_elems + (need_xp ? (size_t)a.w_in : 0)) * sizeof(T) + 16;
-  auto kern = prep_quant_kernel<T, LOG2R, SYL>;
+  // one CTA per token row: 64 threads when there are rows enough to fill the
+  // GPU several times over, 256 (more parallelism per row) for few rows
+  const bool few = a.M < 4 * num_sms();
+  auto kern = few ? prep_quant_kernel<T, LOG2R, SYL, 256> : prep_quant_kernel<T, LOG2R, SYL, 64>;
   if (smem > 220 * 1024) return cudaErrorInvalidValue;   // dynamic + static shared memory must fit 227 KB
   if (smem > 48 * 1024) {
     cudaError_t e = set_smem_once(kern, 220 * 1024);
     if (e != cudaSuccess) return e;
   }
-  kern<<<(unsigned)a.M, kPrepThreads, smem, st>>>(a);
+  kern<<<(unsigned)a.M, few ? 256 : 64, smem, st>>>(a);
   return cudaGetLastError();
 }
 

@@ -80,7 +80,12 @@ __device__ __forceinline__ __half load_scale(const SkinnyArgs& a, int n, int g) 
 
 // 32 activations of token m at k in [k0, k0 + 32), zero past K or M.
 __device__ __forceinline__ void load_x32(const SkinnyArgs& a, int m, long long k0, uint32_t (&w)[16]) {
-  if (m < a.M && k0 + 32 <= a.K && ((a.ldx & 7) == 0)) {
+  if (m >= a.M) {   // token slot past M: zeros, no loads
+#pragma unroll
+    for (int i = 0; i < 16; ++i) w[i] = 0u;
+    return;
+  }
+  if (k0 + 32 <= a.K && ((a.ldx & 7) == 0)) {
     const uint4* p = reinterpret_cast<const uint4*>(a.x + (long long)m * a.ldx + k0);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -98,7 +103,7 @@ __device__ __forceinline__ void load_x32(const SkinnyArgs& a, int m, long long k
 }
 
 template <int TT>
-__global__ void __launch_bounds__(32 * kSkinnyWarps) w4a16_skinny_kernel(const SkinnyArgs a) {
+__global__ void __launch_bounds__(32 * kSkinnyWarps, 2) w4a16_skinny_kernel(const SkinnyArgs a) {
   __shared__ float red[kSkinnyWarps][16][8 * TT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -108,39 +113,58 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps) w4a16_skinny_kernel(const S
 #pragma unroll
   for (int i = 0; i < TT; ++i) d[i][0] = d[i][1] = d[i][2] = d[i][3] = 0.f;
 
-  for (int kb = warp; kb < nkb; kb += kSkinnyWarps) {
-    const uint4 pa = load_packed16(a, n0 + g, kb, t);
-    const uint4 pb = load_packed16(a, n0 + g + 8, kb, t);
-    const int grp = (a.G > 1) ? (kb * 128) / a.group_size : 0;
-    const __half2 sa = __half2half2(load_scale(a, n0 + g, grp));
-    const __half2 sb = __half2half2(load_scale(a, n0 + g + 8, grp));
-    uint32_t xw[TT][16];
+  // The packed weights and scales of PF K blocks per warp are requested
+  // before any of them is used, so each warp has PF HBM loads in flight.
+  constexpr int PF = (TT >= 4) ? 2 : 4;
+  for (int kb0 = warp; kb0 < nkb; kb0 += kSkinnyWarps * PF) {
+    uint4 pa[PF], pb[PF];
+    __half2 sa[PF], sb[PF];
 #pragma unroll
-    for (int i = 0; i < TT; ++i) load_x32(a, i * 8 + g, (long long)kb * 128 + 32 * t, xw[i]);
-    const uint32_t wa[4] = {pa.x, pa.y, pa.z, pa.w};
-    const uint32_t wb[4] = {pb.x, pb.y, pb.z, pb.w};
+    for (int j = 0; j < PF; ++j) {
+      const int kb = kb0 + kSkinnyWarps * j;
+      if (kb < nkb) {
+        pa[j] = load_packed16(a, n0 + g, kb, t);
+        pb[j] = load_packed16(a, n0 + g + 8, kb, t);
+        const int grp = (a.G > 1) ? (kb * 128) / a.group_size : 0;
+        sa[j] = __half2half2(load_scale(a, n0 + g, grp));
+        sb[j] = __half2half2(load_scale(a, n0 + g + 8, grp));
+      } else {
+        pa[j] = pb[j] = make_uint4(0u, 0u, 0u, 0u);
+        sa[j] = sb[j] = __half2half2(__float2half_rn(0.f));
+      }
+    }
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const uint32_t oa = wa[w] ^ 0x88888888u, ob = wb[w] ^ 0x88888888u;
-      const uint32_t xa = oa & 0x0F0F0F0Fu, ya = (oa >> 4) & 0x0F0F0F0Fu;
-      const uint32_t xb = ob & 0x0F0F0F0Fu, yb = (ob >> 4) & 0x0F0F0F0Fu;
+    for (int j = 0; j < PF; ++j) {
+      const int kb = kb0 + kSkinnyWarps * j;
+      if (kb >= nkb) break;
+      uint32_t xw[TT][16];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {   // MMA step s = 2w + h uses k pairs 2h, 2h+1 of word w
-        const int s = 2 * w + h;
-        uint32_t a0, a1, a2, a3;
-        if (a.repacked) {
-          a0 = r16pair_f16(wa[w], 2 * h, sa);
-          a2 = r16pair_f16(wa[w], 2 * h + 1, sa);
-          a1 = r16pair_f16(wb[w], 2 * h, sb);
-          a3 = r16pair_f16(wb[w], 2 * h + 1, sb);
-        } else {
-          a0 = i4pair_f16(xa, ya, 2 * h, sa);
-          a2 = i4pair_f16(xa, ya, 2 * h + 1, sa);
-          a1 = i4pair_f16(xb, yb, 2 * h, sb);
-          a3 = i4pair_f16(xb, yb, 2 * h + 1, sb);
+      for (int i = 0; i < TT; ++i) load_x32(a, i * 8 + g, (long long)kb * 128 + 32 * t, xw[i]);
+      const uint32_t wa[4] = {pa[j].x, pa[j].y, pa[j].z, pa[j].w};
+      const uint32_t wb[4] = {pb[j].x, pb[j].y, pb[j].z, pb[j].w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const uint32_t oa = wa[w] ^ 0x88888888u, ob = wb[w] ^ 0x88888888u;
+        const uint32_t xa = oa & 0x0F0F0F0Fu, ya = (oa >> 4) & 0x0F0F0F0Fu;
+        const uint32_t xb = ob & 0x0F0F0F0Fu, yb = (ob >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {   // MMA step s = 2w + h uses k pairs 2h, 2h+1 of word w
+          const int s = 2 * w + h;
+          uint32_t a0, a1, a2, a3;
+          if (a.repacked) {
+            a0 = r16pair_f16(wa[w], 2 * h, sa[j]);
+            a2 = r16pair_f16(wa[w], 2 * h + 1, sa[j]);
+            a1 = r16pair_f16(wb[w], 2 * h, sb[j]);
+            a3 = r16pair_f16(wb[w], 2 * h + 1, sb[j]);
+          } else {
+            a0 = i4pair_f16(xa, ya, 2 * h, sa[j]);
+            a2 = i4pair_f16(xa, ya, 2 * h + 1, sa[j]);
+            a1 = i4pair_f16(xb, yb, 2 * h, sb[j]);
+            a3 = i4pair_f16(xb, yb, 2 * h + 1, sb[j]);
+          }
+#pragma unroll
+          for (int i = 0; i < TT; ++i) mma_16816(d[i], a0, a1, a2, a3, xw[i][2 * s], xw[i][2 * s + 1]);
         }
-#pragma unroll
-        for (int i = 0; i < TT; ++i) mma_16816(d[i], a0, a1, a2, a3, xw[i][2 * s], xw[i][2 * s + 1]);
       }
     }
   }
@@ -163,6 +187,7 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps) w4a16_skinny_kernel(const S
     __half o16 = __float2half_rn(v);
     if (a.lr_mid) {
       float l = 0.f;
+#pragma unroll 8
       for (int j = 0; j < a.R; ++j)
         l = fmaf(__half2float(a.lr_mid[(long long)m * a.R + j]), __half2float(a.lr_up[(long long)n * a.R + j]), l);
       o16 = __float2half_rn(__half2float(o16) + a.lr_scale * l);
@@ -181,32 +206,67 @@ cudaError_t launch_w4a16_skinny(const SkinnyArgs& a, cudaStream_t st) {
 
 // ------------------------------------------------------------ low rank
 // mid[m, r] = fp16(sum_k x[m, k] * down[r, k]) with fp32 accumulation.
-__global__ void __launch_bounds__(256) lowrank_down_kernel(const __half* x, int K, long long ldx,
+// One CTA per (rank r, tile of 8 tokens): each thread takes 8-value slices
+// of K (16-byte loads of the down row and of the tile's token rows) and the
+// CTA reduces its partial sums in a fixed order (deterministic).
+constexpr int kLrTok = 8;
+__global__ void __launch_bounds__(128) lowrank_down_kernel(const __half* x, int M, int K, long long ldx,
                                                            const __half* down, int R, __half* mid) {
-  extern __shared__ __align__(16) __half xs[];
-  const long long m = blockIdx.x;
-  for (int k = threadIdx.x; k < K; k += 256) xs[k] = x[m * ldx + k];
-  __syncthreads();
+  __shared__ float red[4][kLrTok];
+  const int r = blockIdx.x, m0 = blockIdx.y * kLrTok;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int r = warp; r < R; r += 8) {
-    const __half* dr = down + (long long)r * K;
-    float acc = 0.f;
-    for (int k = lane; k < K; k += 32) acc = fmaf(__half2float(xs[k]), __half2float(dr[k]), acc);
+  const __half* dr = down + (long long)r * K;
+  float acc[kLrTok];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) mid[m * R + r] = __float2half_rn(acc);
+  for (int i = 0; i < kLrTok; ++i) acc[i] = 0.f;
+  const bool vec = ((K & 7) == 0) && ((ldx & 7) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
+                   ((reinterpret_cast<uintptr_t>(down) & 15) == 0);
+  if (vec) {
+    for (int c = threadIdx.x; c < K / 8; c += blockDim.x) {
+      const uint4 dv = __ldg(reinterpret_cast<const uint4*>(dr) + c);
+      const __half2* d2 = reinterpret_cast<const __half2*>(&dv);
+#pragma unroll
+      for (int i = 0; i < kLrTok; ++i) {
+        if (m0 + i >= M) break;
+        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + (long long)(m0 + i) * ldx) + c);
+        const __half2* x2 = reinterpret_cast<const __half2*>(&xv);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 a = __half22float2(x2[j]), b = __half22float2(d2[j]);
+          acc[i] = fmaf(a.x, b.x, fmaf(a.y, b.y, acc[i]));
+        }
+      }
+    }
+  } else {
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+      const float dv = __half2float(dr[k]);
+#pragma unroll
+      for (int i = 0; i < kLrTok; ++i)
+        if (m0 + i < M) acc[i] = fmaf(__half2float(x[(long long)(m0 + i) * ldx + k]), dv, acc[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kLrTok; ++i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < kLrTok; ++i) red[warp][i] = acc[i];
+  }
+  __syncthreads();
+  if (threadIdx.x < kLrTok && m0 + (int)threadIdx.x < M) {
+    const int i = threadIdx.x;
+    const float v = (red[0][i] + red[1][i]) + (red[2][i] + red[3][i]);
+    mid[(long long)(m0 + i) * R + r] = __float2half_rn(v);
   }
 }
 
 cudaError_t launch_lowrank_down(const __half* x, int M, int K, long long ldx, const __half* down, int R,
                                 __half* mid, cudaStream_t st) {
-  const size_t smem = (size_t)K * sizeof(__half);
-  if (smem > 220 * 1024) return cudaErrorInvalidValue;   // dynamic + static shared memory must fit 227 KB
-  if (smem > 48 * 1024) {
-    cudaError_t e = set_smem_once(lowrank_down_kernel, 220 * 1024);
-    if (e != cudaSuccess) return e;
-  }
-  lowrank_down_kernel<<<M, 256, smem, st>>>(x, K, ldx, down, R, mid);
+  if (M == 0) return cudaSuccess;
+  const dim3 grid(R, (M + kLrTok - 1) / kLrTok);
+  lowrank_down_kernel<<<grid, 128, 0, st>>>(x, M, K, ldx, down, R, mid);
   return cudaGetLastError();
 }
 

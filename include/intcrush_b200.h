@@ -114,6 +114,23 @@ int ic_gemm_a8(const int8_t* xq, int64_t M, int64_t K, int64_t ldq,
                const void* bias, int bias_dtype, const float* rowsum, const float* zp_corr,
                void* out, int out_dtype, int64_t ldo, void* stream);
 
+/* Split-K form of ic_gemm_a8 for few output tiles (small M): the K range is
+ * cut into `splits` equal parts (ceil(K/128) % splits == 0; with group scales
+ * also K % group_size == 0 and G % splits == 0), each (tile, part) pair runs
+ * as its own work unit and writes fp32 partials (scaled by s_a and s_w) to
+ * `workspace` ([splits, M, N], at least splits*M*N floats, caller-owned,
+ * contents need not be initialised); a second kernel sums the parts and adds
+ * bias and the zero-point term.  Same result as ic_gemm_a8 up to fp32
+ * summation order.  splits in [1, 16].  Extends fused_int8_gemm_dequant /
+ * fused_w4a8_gemm_dequant (kernels/triton_int8_gemm.py:135-205,
+ * kernels/triton_w4a8_gemm.py:111-169), which have no split-K form. */
+int ic_gemm_a8_splitk(const int8_t* xq, int64_t M, int64_t K, int64_t ldq,
+                      const void* w, int w_kind, int64_t N, int64_t ldw,
+                      const float* s_w, int64_t G, int64_t group_size, const float* s_a,
+                      const void* bias, int bias_dtype, const float* rowsum, const float* zp_corr,
+                      void* out, int out_dtype, int64_t ldo, int splits,
+                      float* workspace, int64_t workspace_elems, void* stream);
+
 /*
  * (a4) W4A16: out = x @ dequant(w)^T with dequant(w)[n,k] = fp16(q[n,k] *
  * s[n, k // group_size]), fp32 accumulation, fused bias and low-rank term

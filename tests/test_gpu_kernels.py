@@ -179,6 +179,44 @@ def test_gemm_a8_zero_point_term():
     assert O.max_rel(out.cpu().numpy(), ref) <= 1e-5
 
 
+@pytest.mark.parametrize("int4,G", [(False, 1), (True, 1), (True, 24), (False, 24)])
+@pytest.mark.parametrize("splits", [2, 3, 4, 6])
+@pytest.mark.parametrize("M", [1, 40, 256])
+def test_gemm_a8_splitk_matches_oracle(int4, G, splits, M):
+    """Split-K (fp32 partials in a workspace + reduce) against the oracle, with
+    bias and the zero-point term; unit scales give the exact integer sums."""
+    dev = _dev()
+    N, K = 320, 3072
+    xq, wq = _int_inputs(M, N, K, seed=M + splits, int4=int4)
+    w = _t(O.pack_int4(wq) if int4 else wq, dev)
+    ones = rt.gemm_a8(_t(xq, dev), w, torch.ones(N, G, device=dev), torch.ones(M, device=dev),
+                      out_dtype=torch.float32, group_size=K // G, splits=splits)
+    assert np.array_equal(ones.cpu().numpy().astype(np.int64), O.int_accumulators(xq, wq)[0])
+    rng = np.random.default_rng(splits)
+    s_w = rng.uniform(1e-3, 2e-2, (N, G)).astype(np.float32)
+    s_a = rng.uniform(1e-3, 5e-2, M).astype(np.float32)
+    bias = (rng.standard_normal(N) * 0.02).astype(np.float16)
+    rowsum = rng.standard_normal(M).astype(np.float32)
+    zpc = (rng.standard_normal(N) * 0.01).astype(np.float32)
+    out = rt.gemm_a8(_t(xq, dev), w, _t(s_w, dev), _t(s_a, dev), bias=_t(bias, dev), out_dtype=torch.float32,
+                     group_size=K // G, rowsum=_t(rowsum, dev), zp_corr=_t(zpc, dev), splits=splits)
+    ref = O.gemm_a8(xq, s_a, wq, s_w if G > 1 else s_w[:, 0], bias=bias, group_size=K // G)
+    ref = ref - rowsum[:, None].astype(np.float64) * zpc[None, :]
+    assert O.max_rel(out.cpu().numpy(), ref) <= 1e-5
+    one = rt.gemm_a8(_t(xq, dev), w, _t(s_w, dev), _t(s_a, dev), bias=_t(bias, dev), out_dtype=torch.float32,
+                     group_size=K // G, rowsum=_t(rowsum, dev), zp_corr=_t(zpc, dev), splits=1)
+    assert O.max_rel(out.cpu().numpy(), one.cpu().numpy().astype(np.float64)) <= 1e-6
+
+
+def test_gemm_a8_splitk_rejects_bad_splits():
+    dev = _dev()
+    M, N, K = 8, 128, 640       # 5 K blocks
+    xq, wq = _int_inputs(M, N, K, seed=1, int4=False)
+    with pytest.raises(Exception):
+        rt.gemm_a8(_t(xq, dev), _t(wq, dev), torch.ones(N, device=dev), torch.ones(M, device=dev),
+                   out_dtype=torch.float32, splits=2)
+
+
 @pytest.mark.parametrize("G", [1, 24])
 @pytest.mark.parametrize("M", [1, 64, 300])
 def test_gemm_a8_repacked_int4_bit_identical(G, M):
