@@ -6,6 +6,8 @@
 #include <string.h>
 #include <math.h>
 
+#include <mutex>
+
 #include "ic_common.cuh"
 
 namespace {
@@ -169,6 +171,61 @@ int ic_gemm_a8_splitk(const int8_t* xq, int64_t M, int64_t K, int64_t ldq, const
                       void* stream) {
   return gemm_a8_impl("ic_gemm_a8_splitk", xq, M, K, ldq, w, w_kind, N, ldw, s_w, G, group_size, s_a, bias,
                       bias_dtype, rowsum, zp_corr, out, out_dtype, ldo, splits, workspace, workspace_elems, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Split-K A8 GEMM without any allocation.
+//
+// Some callers cannot allocate device memory at the moment they run this
+// GEMM: a plain C or FFI host that has no device allocator of its own to hand
+// out a workspace, a process whose device memory is already fully reserved by
+// another framework's pool, or a latency-critical path where cudaMalloc is not
+// allowed because it can synchronise the whole device.  For them the split-K
+// partials live in this file-scope array instead of a caller workspace.  Every
+// GPU that loads the library holds it until the process exits.
+static __device__ __align__(256) float g_splitk_scratch[IC_NOALLOC_SCRATCH_FLOATS];
+
+namespace {
+std::mutex g_scratch_mu;
+float* g_scratch_ptr[64] = {nullptr};   // device address of g_splitk_scratch, per device
+}  // namespace
+
+// Host code sees g_splitk_scratch only as a host-side stand-in: its device
+// address is asked for once per device, with that device current.
+static int scratch_for_current_device(const char* fn, float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(IC_ERR_UNSUPPORTED, "%s: device index %d >= 64", fn, dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_splitk_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress of the split-K scratch");
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return IC_OK;
+}
+
+int ic_gemm_a8_splitk_noalloc(const int8_t* xq, int64_t M, int64_t K, int64_t ldq, const void* w, int w_kind,
+                              int64_t N, int64_t ldw, const float* s_w, int64_t G, int64_t group_size,
+                              const float* s_a, const void* bias, int bias_dtype, const float* rowsum,
+                              const float* zp_corr, void* out, int out_dtype, int64_t ldo, int splits,
+                              void* stream) {
+  const char* fn = "ic_gemm_a8_splitk_noalloc";
+  g_err[0] = 0;
+  if (M < 0 || N < 0 || splits < 1 || splits > 16) return fail(IC_ERR_ARG, "%s: bad M/N/splits", fn);
+  if (splits > 1 && (int64_t)splits * M * N > (int64_t)IC_NOALLOC_SCRATCH_FLOATS)
+    return fail(IC_ERR_ARG, "%s: splits*M*N = %lld exceeds the built-in scratch of %lld floats", fn,
+                (long long)splits * M * N, (long long)IC_NOALLOC_SCRATCH_FLOATS);
+  float* ws = nullptr;
+  if (splits > 1 && M > 0 && N > 0) {
+    const int st = scratch_for_current_device(fn, &ws);
+    if (st != IC_OK) return st;
+  }
+  return gemm_a8_impl(fn, xq, M, K, ldq, w, w_kind, N, ldw, s_w, G, group_size, s_a, bias, bias_dtype, rowsum,
+                      zp_corr, out, out_dtype, ldo, splits, ws, (int64_t)IC_NOALLOC_SCRATCH_FLOATS, stream);
 }
 
 int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const uint8_t* w, int64_t N,

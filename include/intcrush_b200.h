@@ -131,6 +131,30 @@ int ic_gemm_a8_splitk(const int8_t* xq, int64_t M, int64_t K, int64_t ldq,
                       void* out, int out_dtype, int64_t ldo, int splits,
                       float* workspace, int64_t workspace_elems, void* stream);
 
+/* ic_gemm_a8_splitk with no allocation and no caller workspace.  No
+ * counterpart in the reference: it exists for callers that cannot allocate
+ * device memory when they run the GEMM -- a C or FFI host without a device
+ * allocator of its own, a process whose device memory is fully reserved by
+ * another framework's pool, or a path where cudaMalloc is not allowed because
+ * it can synchronise the device.  The partials go to a scratch array built
+ * into the library (IC_NOALLOC_SCRATCH_FLOATS floats = 8 MiB, held on every
+ * GPU that loads the library until the process exits); calls that would need
+ * more (splits * M * N floats) are rejected with IC_ERR_ARG before any work is
+ * queued.  The first call on a device looks up the scratch address for that
+ * device (cudaGetSymbolAddress, with the device current); make that first call
+ * before any stream capture.  Every call shares the one array and the GEMM
+ * overwrites every element the reduce reads, so nothing needs clearing, but
+ * calls whose GPU work overlaps (different streams, or different host threads
+ * on one device) race on it: serialise them.  Arguments as ic_gemm_a8_splitk
+ * without the workspace. */
+#define IC_NOALLOC_SCRATCH_FLOATS 2097152
+int ic_gemm_a8_splitk_noalloc(const int8_t* xq, int64_t M, int64_t K, int64_t ldq,
+                              const void* w, int w_kind, int64_t N, int64_t ldw,
+                              const float* s_w, int64_t G, int64_t group_size, const float* s_a,
+                              const void* bias, int bias_dtype, const float* rowsum,
+                              const float* zp_corr, void* out, int out_dtype, int64_t ldo,
+                              int splits, void* stream);
+
 /*
  * (a4) W4A16: out = x @ dequant(w)^T with dequant(w)[n,k] = fp16(q[n,k] *
  * s[n, k // group_size]), fp32 accumulation, fused bias and low-rank term
