@@ -131,6 +131,14 @@ def run_reference(args, rank: int) -> None:
 
 # ───────────────────────────── GPU arm ──────────────────────────────────────
 
+def _gpu_head_start(ms: float = 10.0) -> None:
+    """Keep the GPU busy for ~ms before a timed loop (outside its events) so
+    that the host queues the loop's launches ahead of the GPU: the per-step
+    events then time GPU work, not host launch latency."""
+    import torch
+    torch.cuda._sleep(int(ms * 1e-3 * 2.0e9))
+
+
 class Clocks:
     """Samples nvidia-smi during the timed region."""
 
@@ -140,13 +148,16 @@ class Clocks:
         self.path = os.path.join("/tmp", f"ic_clocks_{os.getpid()}.csv")
 
     def __enter__(self):
+        if os.environ.get("INTCRUSH_NO_CLOCKS"):
+            return self
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.idx), "--query-gpu=clocks.sm,clocks.max.sm,power.draw,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "20"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "--format=csv,noheader,nounits", "-lms", os.environ.get("INTCRUSH_CLOCK_MS", "100")],
+                stdout=self.f, stderr=subprocess.DEVNULL)
             # the sampler needs a moment to start: wait for its first row so that
             # short timed regions are covered too
             t0 = time.time()
@@ -178,6 +189,8 @@ class Clocks:
             self.f.close()
 
     def summary(self):
+        if os.environ.get("INTCRUSH_NO_CLOCKS"):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "sampling disabled"}
         try:
             rows = [r.split(",") for r in open(self.path).read().strip().splitlines() if r.strip()]
             sm = sorted(float(r[0]) for r in rows)
@@ -217,6 +230,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         dist.barrier()
     torch.cuda.synchronize()
     with Clocks(local_rank) as clk:
+        _gpu_head_start()   # after the sampler is up
+        for i in range(2):   # untimed: the first steps after an idle GPU run slow
+            flush.fill_(float(i))
+            step(d["x"])
         t_wall = time.perf_counter()
         for i in range(args.steps):
             flush.fill_(float(i))
@@ -232,6 +249,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         dist.barrier()
     prep_ms = [ev[i][0].elapsed_time(ev[i][1]) for i in range(args.steps)]
     gemm_ms = [ev[i][1].elapsed_time(ev[i][2]) for i in range(args.steps)]
+    if os.environ.get("INTCRUSH_BENCH_DEBUG"):
+        print(f"rank {rank} dev {torch.cuda.current_device()} gemm_ms {[round(v, 3) for v in gemm_ms]} "
+              f"prep_ms {[round(v, 3) for v in prep_ms]}", file=sys.stderr, flush=True)
     tot_ms = sum(prep_ms) + sum(gemm_ms)
 
     # e2e: host-pinned input in, host-pinned output out, through the runtime
@@ -350,6 +370,10 @@ def run_features(args, rank: int, world: int, local_rank: int) -> None:
         dist.barrier()
     torch.cuda.synchronize()
     with Clocks(local_rank) as clk:
+        _gpu_head_start()   # after the sampler is up
+        for i in range(2):   # untimed: the first steps after an idle GPU run slow
+            flush.fill_(float(i))
+            lin(d["x"])
         for i in range(args.steps):
             flush.fill_(float(i))
             ev[i][0].record(st)
@@ -556,6 +580,10 @@ def run_block(args, rank: int, world: int, local_rank: int) -> None:
             dist.barrier()
         torch.cuda.synchronize()
         with Clocks(local_rank) as clk:
+            _gpu_head_start()   # after the sampler is up
+            for i in range(2):   # untimed: the first steps after an idle GPU run slow
+                flush.fill_(float(i))
+                blk(img, txt, vec)
             for i in range(args.steps):
                 flush.fill_(float(i))
                 ev[i][0].record(st)
