@@ -372,10 +372,9 @@ static cudaError_t launch_prep_t(const PrepArgs& a, cudaStream_t st) {
   const bool need_xp = (a.perm != nullptr) || (a.smooth != nullptr);
   const size_t xr_elems = (size_t)((a.Wp + 7) & ~7LL);
   const size_t smem = buf_bytes + (xr_elems + (need_xp ? (size_t)a.w_in : 0)) * sizeof(T) + 16;
-  // one CTA per token row: 64 threads for short rows (<= 4096 values) when
-  // there are rows enough to fill the GPU several times over; 256 (more
-  // parallelism per row) for few rows or wide rows
-  const bool few = a.M < 4 * num_sms() || a.Wp > 4096;
+  // one CTA per token row: 64 threads when there are rows enough to fill the
+  // GPU several times over, 256 (more parallelism per row) for few rows
+  const bool few = a.M < 4 * num_sms();
   auto kern = few ? prep_quant_kernel<T, LOG2R, SYL, 256> : prep_quant_kernel<T, LOG2R, SYL, 64>;
   if (smem > 220 * 1024) return cudaErrorInvalidValue;   // dynamic + static shared memory must fit 227 KB
   if (smem > 48 * 1024) {
