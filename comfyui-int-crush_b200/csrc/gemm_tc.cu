@@ -86,7 +86,9 @@ struct Cfg {
   static constexpr bool I4 = (MODE != W_I8);
   // epilogue warps: group-scaled tiles keep 64 fp32 accumulators per thread
   // (one warp per 32 TMEM lanes x 64 columns); per-channel tiles stream.
-  static constexpr int EPI = GROUPED ? (BN >= 64 ? BN / 16 : 4) : ((BN > 128) ? 8 : 4);
+  // (BN = 160, group-scaled: 8 warps of 80 columns, so that three accumulator
+  // buffers fit in tensor memory)
+  static constexpr int EPI = GROUPED ? (BN == 160 ? 8 : (BN >= 64 ? BN / 16 : 4)) : ((BN > 128) ? 8 : 4);
   static constexpr int CPT = BN / (EPI / 4);                      // columns per epilogue thread
   static constexpr int THREADS = 32 * (4 + EPI);
   static constexpr int W_BYTES = kTileN * 128;                    // 16 KB
@@ -94,7 +96,7 @@ struct Cfg {
   static constexpr int P_BYTES = (MODE == W_I4) ? kTileN * 64 : (MODE == W_I4F ? kTileN * 32 : 0);
   // group-scaled tiles: four accumulator buffers when they fit in TMEM, and
   // two 1 KB constant atoms (the operands of the re-arming MMA) at offset 0
-  static constexpr int NBUF = (GROUPED && BN <= 128) ? 4 : 2;
+  static constexpr int NBUF = (GROUPED && BN <= 128) ? 4 : ((GROUPED && BN == 160) ? 3 : 2);
   static constexpr int MAGIC_BYTES = GROUPED ? 2048 : 0;
   static constexpr int BUDGET = 224 * 1024 - MAGIC_BYTES;
   static constexpr int S_P = I4 ? 8 : 0;   // even: the two expansion warps own alternate stages
@@ -112,7 +114,7 @@ struct Cfg {
   static constexpr int SMEM = OFF_BAR + 512 + 1024;               // barriers + alignment slack
   static constexpr int KB_ELEMS = (MODE == W_I4F) ? 64 : 128;     // K elements per block
   static_assert(EPI % 4 == 0, "epilogue warps cover the four TMEM lane quarters evenly");
-  static_assert(CPT % 32 == 0, "epilogue columns per thread must be a multiple of 32");
+  static_assert(CPT % 32 == 0 || (GROUPED && CPT % 16 == 0), "epilogue column slices of 32 (16 at the end)");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
   static_assert(S_X >= 2, "pipeline depth");
   static_assert(!(GROUPED && MODE == W_I4F), "W4A16 folds scales into the weights");
@@ -185,11 +187,11 @@ __device__ __forceinline__ void acc2_magic(float& a0, float& a1, uint32_t r0, ui
 // per-token factors of token m0 + j (coalesced) and shuffles them to all.
 template <typename T>
 __device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const float* v, int m0, int n,
-                                              bool nvalid, float bias_n, float zpc_n, int lane) {
+                                              bool nvalid, float bias_n, float zpc_n, int lane, int width) {
   const int ml = m0 + lane;
   const float sa_l = (ml < a.M) ? __ldg(&a.s_a[ml]) : 0.f;
   const float rs_l = (a.rowsum && ml < a.M) ? __ldg(&a.rowsum[ml]) : 0.f;
-  const int jmax = nvalid ? min(32, a.M - m0) : 0;   // valid tokens in this chunk
+  const int jmax = nvalid ? min(width, a.M - m0) : 0;   // valid tokens in this chunk
   T* p = out + (size_t)m0 * a.ldo + n;
   float sa_b = sa_l, rs_b = rs_l;
 #pragma unroll
@@ -210,22 +212,22 @@ __device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const f
 }
 
 __device__ __forceinline__ void store_chunk(const GemmArgs& a, const float* v, int m0, int n, bool nvalid,
-                                            float bias_n, float zpc_n, int lane) {
+                                            float bias_n, float zpc_n, int lane, int width = 32) {
   if (a.out_dtype == IC_DTYPE_F16)
-    store_chunk_t(a, reinterpret_cast<__half*>(a.out), v, m0, n, nvalid, bias_n, zpc_n, lane);
+    store_chunk_t(a, reinterpret_cast<__half*>(a.out), v, m0, n, nvalid, bias_n, zpc_n, lane, width);
   else if (a.out_dtype == IC_DTYPE_BF16)
-    store_chunk_t(a, reinterpret_cast<__nv_bfloat16*>(a.out), v, m0, n, nvalid, bias_n, zpc_n, lane);
+    store_chunk_t(a, reinterpret_cast<__nv_bfloat16*>(a.out), v, m0, n, nvalid, bias_n, zpc_n, lane, width);
   else
-    store_chunk_t(a, reinterpret_cast<float*>(a.out), v, m0, n, nvalid, bias_n, zpc_n, lane);
+    store_chunk_t(a, reinterpret_cast<float*>(a.out), v, m0, n, nvalid, bias_n, zpc_n, lane, width);
 }
 
 // Split-K partial of 32 consecutive tokens of feature n:
 // ws[split, m, n] = v[j] * s_a[m] (fp32; bias and zero point come in the reduce).
 __device__ __forceinline__ void store_partial(const GemmArgs& a, const float* v, int split, int m0, int n,
-                                              bool nvalid, int lane) {
+                                              bool nvalid, int lane, int width = 32) {
   const int ml = m0 + lane;
   const float sa_b = (ml < a.M) ? __ldg(&a.s_a[ml]) : 0.f;
-  const int jmax = nvalid ? min(32, a.M - m0) : 0;
+  const int jmax = nvalid ? min(width, a.M - m0) : 0;
   float* p = a.ws + ((size_t)split * a.M + m0) * a.N + n;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
@@ -619,33 +621,42 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           tc_fence_after();
           // read the whole buffer, then hand it back at once: the MMA warp
           // re-arms it itself, so nothing is written to tensor memory here
-          uint32_t r[C::CPT / 32][32];
+          constexpr int C32 = C::CPT / 32, C16 = (C::CPT % 32) / 16;
+          uint32_t r[C32][32];
+          uint32_t r16[C16 ? 16 : 1];
 #pragma unroll
-          for (int c = 0; c < C::CPT / 32; ++c)
+          for (int c = 0; c < C32; ++c)
             tmem_ld32(tmem_base + lane_base + (uint32_t)(b * BN + col0 + 32 * c), r[c]);
+          if constexpr (C16 > 0) tmem_ld16(tmem_base + lane_base + (uint32_t)(b * BN + col0 + 32 * C32), r16);
           tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[b]);
           const unsigned long long sw2 = pack2(sw, sw);
 #pragma unroll
-          for (int c = 0; c < C::CPT / 32; ++c)
+          for (int c = 0; c < C32; ++c)
 #pragma unroll
             for (int j = 0; j < 16; ++j) acc2p(accp[16 * c + j], r[c][2 * j], r[c][2 * j + 1], sw2, mg2);
+          if constexpr (C16 > 0) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc2p(accp[16 * C32 + j], r16[2 * j], r16[2 * j + 1], sw2, mg2);
+          }
           if (warp == 4 && lane == 0) IC_TADD(4);
           sw = sw_next;
         }
         if (!ok) break;
 #pragma unroll
-        for (int c = 0; c < C::CPT / 32; ++c) {
+        for (int c = 0; c < (C::CPT + 31) / 32; ++c) {
+          const int width = (32 * c + 32 <= C::CPT) ? 32 : 16;   // a last slice of 16 when CPT % 32 == 16
           float v[32];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            v[2 * j] = __uint_as_float((uint32_t)accp[16 * c + j]);
-            v[2 * j + 1] = __uint_as_float((uint32_t)(accp[16 * c + j] >> 32));
+            const bool in = 16 * c + j < C::CPT / 2;
+            v[2 * j] = in ? __uint_as_float((uint32_t)accp[in ? 16 * c + j : 0]) : 0.f;
+            v[2 * j + 1] = in ? __uint_as_float((uint32_t)(accp[in ? 16 * c + j : 0] >> 32)) : 0.f;
           }
-          if (a.splits > 1) store_partial(a, v, split, mbase + 32 * c, n, nvalid, lane);
-          else store_chunk(a, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane);
+          if (a.splits > 1) store_partial(a, v, split, mbase + 32 * c, n, nvalid, lane, width);
+          else store_chunk(a, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane, width);
         }
       } else {
         const int b = uc % NB;
@@ -775,6 +786,9 @@ static cudaError_t dispatch_bn(int bn, const CUtensorMap& tw, const CUtensorMap&
     case 32: return launch_gemm_t<MODE, 32, GROUPED>(tw, tx, a, st);
     case 64: return launch_gemm_t<MODE, 64, GROUPED>(tw, tx, a, st);
     case 128: return launch_gemm_t<MODE, 128, GROUPED>(tw, tx, a, st);
+    case 160:
+      if constexpr (GROUPED) return launch_gemm_t<MODE, 160, GROUPED>(tw, tx, a, st);
+      else return cudaErrorInvalidValue;
     case 192:
       if constexpr (GROUPED) return launch_gemm_t<MODE, 192, GROUPED>(tw, tx, a, st);
       else return cudaErrorInvalidValue;

@@ -385,9 +385,282 @@ static cudaError_t launch_prep_t(const PrepArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+constexpr int kPwBufDoubles = 512 + 32;   // per-warp fp64 exchange buffer (pidx(511) = 542)
+
+__device__ __forceinline__ int8_t quant1(float xv, float s, float rs) {
+  // q = rint(x / s) with the quotient correctly rounded to fp32: x * (1/s) is
+  // within 2 fp32 ulps of it, so both round to the same integer unless the
+  // product lies within 2^-21 (relative) of a half-integer; then the exact
+  // division is evaluated.  1.5 * 2^23 rounds to nearest, ties to even.
+  float y = xv * rs;
+  const float fy = fabsf(y);
+  if (fabsf(fy - (floorf(fy) + 0.5f)) <= fy * 4.8e-7f) y = __fdiv_rn(xv, s);
+  return (int8_t)max(-128, min(127, __float_as_int(y + 12582912.0f) - 0x4B400000));
+}
+
+// INTCRUSH_PREP_V1=1 routes every request to prep_quant_kernel (tests use it
+// to check the two kernels against each other).
+static bool prep_v1_forced() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("INTCRUSH_PREP_V1");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+// ---------------------------------------------------------------------------
+// prep_row_kernel: rotation sizes 16..256 without SmoothQuant divide (the
+// W4A8 / SmoothRot layout).  Persistent 256-thread CTAs loop over rows; the
+// arithmetic and the results are those of prep_quant_kernel (bit-identical),
+// with less work per value and one CTA barrier per row in the hot path:
+//  * each warp rotates whole 512-value chunks of the row on its own: lane l
+//    loads 16 consecutive inputs, applies the butterflies of index bits 0-3 in
+//    fp64 registers, exchanges through a warp-private fp64 buffer, finishes
+//    the remaining bits and writes the once-rounded values to the row buffer;
+//  * the SmoothRot quotient fp16(x / fp16(f)) is x * (1 / fp16(f)) from a
+//    per-CTA reciprocal table, except within 4 fp32 ulps of a rounding
+//    midpoint of the activation dtype, where the IEEE division is evaluated
+//    (the product is within 2 ulps of the correctly rounded quotient, so
+//    elsewhere both round to the same value);
+//  * the PermuQuant gather runs once: the gathered values stay in registers
+//    for the absmax, the optional prepped row / row sum and the quantisation.
+constexpr int kRowThreads = 256;
+constexpr int kRowWarps = kRowThreads / 32;
+
+template <typename T> struct MidBits;
+template <> struct MidBits<__half> {          // 10-bit mantissa: 13 fp32 bits below it
+  static constexpr uint32_t MASK = 0x1FFFu, MID = 0x1000u;
+  static constexpr float MIN_NORMAL = 6.103515625e-05f, MAX = 65504.0f;
+};
+template <> struct MidBits<__nv_bfloat16> {   // 7-bit mantissa: 16 fp32 bits below it
+  static constexpr uint32_t MASK = 0xFFFFu, MID = 0x8000u;
+  static constexpr float MIN_NORMAL = 1.1754943508e-38f, MAX = 3.38e38f;
+};
+
+// fp16-rounded (or bf16-rounded) quotient x / f given r = RN(1 / f).
+// (fp32 factor f[k] read from global memory only on the exact path)
+template <typename T>
+__device__ __forceinline__ float smoothrot_div(float x, const float* fg, int k, float r) {
+  const float y = x * r;
+  const float ay = fabsf(y);
+  const uint32_t low = __float_as_uint(y) & MidBits<T>::MASK;
+  const uint32_t d = low > MidBits<T>::MID ? low - MidBits<T>::MID : MidBits<T>::MID - low;
+  float q = y;
+  if (d <= 4u || ay < MidBits<T>::MIN_NORMAL || ay > MidBits<T>::MAX)
+    q = __fdiv_rn(x, DT<T>::to_f(DT<T>::from_f(__ldg(fg + k))));
+  return DT<T>::to_f(DT<T>::from_f(q));
+}
+
+template <typename T, int LOG2R, bool SYL, int MAXIT>
+__global__ void __launch_bounds__(kRowThreads) prep_row_kernel(const PrepArgs a, int xr_stride) {
+  static_assert(LOG2R >= 4 && LOG2R <= 8, "prep_row_kernel covers rotation sizes 16..256");
+  constexpr int R = 1 << LOG2R;
+  constexpr int HB = LOG2R - 4;            // index bits of the second pass
+  constexpr int NE = 1 << HB;              // values per second-pass group
+  constexpr int GPL = 16 / NE;             // second-pass groups per lane
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ float red[2][kRowWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K = (int)a.K, Kr = (int)a.Kr, Wp = (int)a.Wp, w_in = (int)a.w_in, ldq = (int)a.ldq;
+  double* buf = reinterpret_cast<double*>(smem) + warp * kPwBufDoubles;
+  T* xr = reinterpret_cast<T*>(smem + kRowWarps * kPwBufDoubles * 8);
+  float* sr = reinterpret_cast<float*>(smem + kRowWarps * kPwBufDoubles * 8 + (size_t)xr_stride * sizeof(T));
+  const double scale = SYL ? a.syl_h : 1.0 / (double)(1 << (LOG2R / 2));
+  const bool vperm = a.perm && ((w_in & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.perm) & 15) == 0);
+
+  // reciprocals of the SmoothRot factors rounded to the activation dtype
+  if (a.smoothrot) {
+    for (int k = threadIdx.x; k < K; k += kRowThreads) sr[k] = __frcp_rn(DT<T>::to_f(DT<T>::from_f(a.smoothrot[k])));
+  }
+  __syncthreads();
+
+  for (int64_t row = blockIdx.x; row < a.M; row += gridDim.x) {
+    const T* xrow = reinterpret_cast<const T*>(a.x) + row * a.ldx;
+    // ---- rotation into xr[0, Kr): warp w takes chunks w, w + 8, ...
+    for (int c0 = warp * 512; c0 < Kr; c0 += kRowWarps * 512) {
+      const int e0 = c0 + 16 * lane;
+      if (e0 < Kr) {
+        uint4 r0, r1;
+        if (a.vec_ok && e0 + 16 <= K) {
+          const uint4* p = reinterpret_cast<const uint4*>(xrow + e0);
+          r0 = __ldg(p);
+          r1 = __ldg(p + 1);
+        } else {
+          T t[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) t[j] = (e0 + j < K) ? xrow[e0 + j] : DT<T>::from_f(0.f);
+          r0 = *reinterpret_cast<const uint4*>(&t[0]);
+          r1 = *reinterpret_cast<const uint4*>(&t[8]);
+        }
+        const T* t0 = reinterpret_cast<const T*>(&r0);
+        const T* t1 = reinterpret_cast<const T*>(&r1);
+        double v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float f = DT<T>::to_f(j < 8 ? t0[j] : t1[j - 8]);
+          if (a.smoothrot && e0 + j < K) f = smoothrot_div<T>(f, a.smoothrot, e0 + j, sr[e0 + j]);
+          v[j] = (double)f;
+        }
+        butterflies<4, SYL, double>(v);
+        if constexpr (HB == 0) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) xr[e0 + j] = DT<T>::from_d(v[j] * scale);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) buf[pidx(16 * lane + j)] = v[j];
+        }
+      }
+      if constexpr (HB > 0) {
+        __syncwarp();
+#pragma unroll
+        for (int gi = 0; gi < GPL; ++gi) {
+          const int q = lane * GPL + gi;         // group: block q / 16, low bits q % 16
+          const int base = (q >> 4) * R + (q & 15);
+          if (c0 + base < Kr) {
+            double v[NE];
+#pragma unroll
+            for (int h = 0; h < NE; ++h) v[h] = buf[pidx(base + 16 * h)];
+            butterflies<HB, SYL, double>(v);
+#pragma unroll
+            for (int h = 0; h < NE; ++h) xr[c0 + base + 16 * h] = DT<T>::from_d(v[h] * scale);
+          }
+        }
+        __syncwarp();
+      }
+    }
+    for (int k = Kr + threadIdx.x; k < Wp; k += kRowThreads) xr[k] = DT<T>::from_f(0.f);
+    __syncthreads();
+
+    // ---- gather (once): thread t holds outputs 4t + 1024 i .. + 3
+    float g[MAXIT][4];
+    float amax = 0.f, rsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXIT; ++i) {
+      const int j0 = 4 * threadIdx.x + 1024 * i;
+      int src[4] = {j0, j0 + 1, j0 + 2, j0 + 3};
+      if (a.perm) {
+        if (vperm && j0 + 4 <= w_in) {
+          const int4 p = __ldg(reinterpret_cast<const int4*>(a.perm + j0));
+          src[0] = p.x; src[1] = p.y; src[2] = p.z; src[3] = p.w;
+        } else {
+#pragma unroll
+          for (int t = 0; t < 4; ++t) src[t] = (j0 + t < w_in) ? a.perm[j0 + t] : 0;
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        g[i][t] = (j0 + t < w_in) ? DT<T>::to_f(xr[src[t]]) : 0.f;
+        amax = fmaxf(amax, fabsf(g[i][t]));
+        rsum += g[i][t];
+      }
+      if (a.x_prep && j0 < w_in) {
+        T* dst = reinterpret_cast<T*>(a.x_prep) + row * (int64_t)w_in + j0;
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          if (j0 + t < w_in) dst[t] = DT<T>::from_f(g[i][t]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      rsum += __shfl_xor_sync(0xffffffffu, rsum, o);
+    }
+    if (lane == 0) {
+      red[0][warp] = amax;
+      red[1][warp] = rsum;
+    }
+    __syncthreads();
+    amax = red[0][0];
+    rsum = red[1][0];
+#pragma unroll
+    for (int w = 1; w < kRowWarps; ++w) {
+      amax = fmaxf(amax, red[0][w]);
+      rsum += red[1][w];
+    }
+    if (a.rowsum && threadIdx.x == 0) a.rowsum[row] = rsum;
+
+    // ---- quantise from registers: 4 bytes per thread per step
+    if (a.xq) {
+      const float s = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
+      const float rs = __frcp_rn(s);
+      if (threadIdx.x == 0) a.s_a[row] = s;
+      int8_t* qrow = a.xq + row * a.ldq;
+#pragma unroll
+      for (int i = 0; i < MAXIT; ++i) {
+        const int j0 = 4 * threadIdx.x + 1024 * i;
+        if (j0 < ldq) {
+          uint32_t word = 0;
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int8_t qv = (j0 + t < w_in) ? quant1(g[i][t], s, rs) : (int8_t)0;
+            word |= ((uint32_t)(uint8_t)qv) << (8 * t);
+          }
+          *reinterpret_cast<uint32_t*>(qrow + j0) = word;
+        }
+      }
+    }
+    __syncthreads();   // red and xr are rewritten by the next row
+  }
+}
+
+template <typename T, int LOG2R, bool SYL>
+static cudaError_t launch_prep_row(const PrepArgs& a, cudaStream_t st) {
+  const int xr_stride = (int)((a.Wp + 15) & ~15LL);
+  const size_t kpad = (size_t)((a.K + 3) & ~3LL);
+  const size_t smem = (size_t)kRowWarps * kPwBufDoubles * 8 + (size_t)xr_stride * sizeof(T) +
+                      (a.smoothrot ? kpad * sizeof(float) : 0);
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  const int its = (int)((a.ldq + 1023) / 1024);
+  cudaError_t e;
+  int per_sm = 0;
+  auto go = [&](auto kern) -> cudaError_t {
+    if (smem > 48 * 1024) {
+      cudaError_t e2 = set_smem_once(kern, 220 * 1024);
+      if (e2 != cudaSuccess) return e2;
+    }
+    cudaError_t e2 = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRowThreads, smem);
+    if (e2 != cudaSuccess) return e2;
+    if (per_sm < 1) per_sm = 1;
+    const int64_t cap = (int64_t)per_sm * num_sms();
+    const unsigned grid = (unsigned)(a.M < cap ? a.M : cap);
+    kern<<<grid, kRowThreads, smem, st>>>(a, xr_stride);
+    return cudaGetLastError();
+  };
+  if (its <= 4) e = go(prep_row_kernel<T, LOG2R, SYL, 4>);
+  else if (its <= 16) e = go(prep_row_kernel<T, LOG2R, SYL, 16>);
+  else e = cudaErrorInvalidValue;
+  return e;
+}
+
+// Whether prep_row_kernel takes this request.
+static bool prep_row_fits(const PrepArgs& a, int log2r, size_t tsize) {
+  // measured: faster for few rows (4.5 vs 5.7 us for one row); for thousands
+  // of rows prep_quant_kernel is faster (68 vs 78 us for 4096 x 3072)
+  static const int force_row = [] { const char* e = getenv("INTCRUSH_PREP_ROW"); return (e && e[0] == '1') ? 1 : 0; }();
+  if (log2r < 4 || log2r > 8 || a.smooth || a.M == 0) return false;
+  // many short rows: prep_quant_kernel (68 vs 78 us at 4096 x 3072); few rows
+  // or wide rows: this kernel
+  if (a.M >= 4 * num_sms() && a.Wp <= 4096 && !force_row) return false;
+  if ((a.ldq + 1023) / 1024 > 16) return false;
+  const size_t smem = (size_t)kRowWarps * kPwBufDoubles * 8 + (size_t)((a.Wp + 15) & ~15LL) * tsize +
+                      (a.smoothrot ? (size_t)((a.K + 3) & ~3LL) * sizeof(float) : 0);
+  return smem <= 200 * 1024 && !prep_v1_forced();
+}
+
 template <typename T>
 static cudaError_t launch_prep_dt(const PrepArgs& a, int log2r, bool syl, cudaStream_t st) {
   if (log2r == 0) return launch_prep_t<T, 0, false>(a, st);
+  if (prep_row_fits(a, log2r, sizeof(T))) {
+    if (syl) {
+      if (log2r == 5) return launch_prep_row<T, 5, true>(a, st);
+      if (log2r == 7) return launch_prep_row<T, 7, true>(a, st);
+    } else {
+      if (log2r == 4) return launch_prep_row<T, 4, false>(a, st);
+      if (log2r == 6) return launch_prep_row<T, 6, false>(a, st);
+      if (log2r == 8) return launch_prep_row<T, 8, false>(a, st);
+    }
+  }
   if (!syl) {
     switch (log2r) {
       case 2: return launch_prep_t<T, 2, false>(a, st);

@@ -56,6 +56,7 @@ PREP_CASES = [
     (2500, 3072, 256, 3072, True, True, False),    # more rows than resident warps
     (5, 1000, 16, 1010, True, False, True),        # ragged K and w_in (scalar gather)
     (3, 9000, 64, 9024, True, True, False),        # long row in the per-warp buffer
+    (600, 12288, 256, 12288, True, True, False),   # many wide rows (row kernel route)
 ]
 
 
@@ -79,6 +80,37 @@ def test_prep_quant_bit_exact(M, K, rot, w_in, use_perm, use_sr, use_sm):
     assert np.array_equal(s_a.cpu().numpy(), s_ref), "scales differ"
     assert np.array_equal(xq.cpu().numpy(), q_ref), "int8 activations differ"
     np.testing.assert_allclose(rs.cpu().numpy(), ref.astype(np.float64).sum(1), rtol=1e-3, atol=1e-2)
+
+
+def test_prep_both_kernels_bit_identical():
+    """Few rows take prep_row_kernel, many rows prep_quant_kernel; with
+    INTCRUSH_PREP_V1=1 every request takes prep_quant_kernel.  Both give the
+    same bits (fresh processes, the switch is read once)."""
+    import subprocess, sys, os
+    _dev()
+    code = (
+        "import sys; sys.path[:0] = %r\n"
+        "import conftest, numpy as np, torch, intcrush_oracle as O\n"
+        "from _pkg import load\n"
+        "rt = load('_b200_runtime')\n"
+        "rng = np.random.default_rng(3)\n"
+        "x = torch.from_numpy((rng.standard_normal((100, 3000)) * 3).astype(np.float16)).cuda()\n"
+        "sr = torch.from_numpy(rng.uniform(0.5, 4, 3000).astype(np.float32)).cuda()\n"
+        "perm = torch.from_numpy(rng.permutation(3072).astype(np.int32)).cuda()\n"
+        "q, s, xp, rs = rt.prep_quantize(x, smoothrot=sr, rot_size=256, w_in=3072, perm=perm, want_prep=True)\n"
+        "np.save(sys.argv[1], np.concatenate([q.cpu().numpy().view(np.uint8).ravel(), s.cpu().numpy().view(np.uint8),"
+        " xp.cpu().numpy().view(np.uint8).ravel()]))\n"
+    ) % ([os.path.dirname(__file__)],)
+    import tempfile
+    outs = []
+    for v1 in ("0", "1"):
+        f = tempfile.mktemp(suffix=".npy")
+        env = dict(os.environ, INTCRUSH_PREP_V1=v1)
+        r = subprocess.run([sys.executable, "-c", code, f], env=env, capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        outs.append(np.load(f))
+        os.remove(f)
+    assert np.array_equal(outs[0], outs[1])
 
 
 def test_prep_bf16_runs_and_matches_fp16_semantics():
@@ -248,7 +280,7 @@ def test_w4a16_repacked_bit_identical(M):
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("bn", [32, 64, 128, 192, 256])
+@pytest.mark.parametrize("bn", [32, 64, 128, 160, 192, 256])
 def test_gemm_a8_grouped_every_tile_width(bn, monkeypatch):
     """Each token-tile width of the group-scale kernel, in a fresh process."""
     import subprocess, sys, os
