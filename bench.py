@@ -493,10 +493,10 @@ class _QLinear:
         self.b = (torch.randn(n_out, generator=g) * 0.02).half().to(dev)
         self.n_in = n_in
 
-    def __call__(self, x):
-        import torch
+    def __call__(self, x, norm=None):
         x2 = x.reshape(-1, x.shape[-1])
-        xq, s_a, _, _ = self.rt.prep_quantize(x2, smoothrot=self.sr, rot_size=ROT, w_in=self.n_in, perm=self.perm)
+        xq, s_a, _, _ = self.rt.prep_quantize(x2, smoothrot=self.sr, rot_size=ROT, w_in=self.n_in, perm=self.perm,
+                                              norm=norm)
         y = self.rt.gemm_a8(xq, self.w, self.s, s_a, bias=self.b, out_dtype=x.dtype, group_size=GS, repacked=True)
         return y.reshape(*x.shape[:-1], y.shape[-1])
 
@@ -506,11 +506,17 @@ class FluxDoubleBlock:
     24 heads x 128, MLP 12288 GELU(tanh), adaLN modulation from a 3072-d
     vector, separate image / text weights, joint attention over text + image
     tokens.  Every linear is the quantised layer above; norms, modulation,
-    GELU and attention (torch SDPA) run in fp16.  Random-init weights."""
+    GELU and attention (torch SDPA) run in fp16.  Random-init weights.
 
-    def __init__(self, rt, dev, seed=0, hidden=3072, heads=24, mlp=12288):
+    With ``fused_norm`` (default) the pre-attention and pre-MLP LayerNorm
+    (eps 1e-6, no affine) and the adaLN modulation ``(1 + scale) * x + shift``
+    run inside the quantised layer's prep kernel as a LayerNorm with
+    per-sample gamma = 1 + scale, beta = shift (batch 1)."""
+
+    def __init__(self, rt, dev, seed=0, hidden=3072, heads=24, mlp=12288, fused_norm=True):
         import torch
         g = torch.Generator().manual_seed(seed)
+        self.fused_norm = fused_norm
         self.h, self.nh = hidden, heads
         mk = lambda o, i: _QLinear(rt, o, i, g, dev)
         self.mod = {s: mk(6 * hidden, hidden) for s in ("img", "txt")}
@@ -536,8 +542,11 @@ class FluxDoubleBlock:
         qs, ks, vv = [], [], []
         for s, x in (("txt", txt), ("img", img)):
             sh, sc, _, _, _, _ = mods[s]
-            xn = F.layer_norm(x, (h,)) * (1 + sc[:, None]) + sh[:, None]
-            q, k, v = self.qkv[s](xn).view(B, -1, 3, nh, h // nh).permute(2, 0, 3, 1, 4)
+            if self.fused_norm:
+                qkv = self.qkv[s](x, norm=("layer", (1 + sc[0]).float(), sh[0].float(), 1e-6))
+            else:
+                qkv = self.qkv[s](F.layer_norm(x, (h,), eps=1e-6) * (1 + sc[:, None]) + sh[:, None])
+            q, k, v = qkv.view(B, -1, 3, nh, h // nh).permute(2, 0, 3, 1, 4)
             q = F.rms_norm(q, (h // nh,), self.qn[s])
             k = F.rms_norm(k, (h // nh,), self.kn[s])
             qs.append(q); ks.append(k); vv.append(v)
@@ -548,8 +557,11 @@ class FluxDoubleBlock:
         for s, x, att in (("txt", txt, a[:, :nt]), ("img", img, a[:, nt:])):
             _, _, g1, sh2, sc2, g2 = mods[s]
             x = x + g1[:, None] * self.proj[s](att)
-            xn = F.layer_norm(x, (h,)) * (1 + sc2[:, None]) + sh2[:, None]
-            x = x + g2[:, None] * self.fc2[s](F.gelu(self.fc1[s](xn), approximate="tanh"))
+            if self.fused_norm:
+                f1 = self.fc1[s](x, norm=("layer", (1 + sc2[0]).float(), sh2[0].float(), 1e-6))
+            else:
+                f1 = self.fc1[s](F.layer_norm(x, (h,), eps=1e-6) * (1 + sc2[:, None]) + sh2[:, None])
+            x = x + g2[:, None] * self.fc2[s](F.gelu(f1, approximate="tanh"))
             outs.append(x)
         return outs[1], outs[0]
 
@@ -564,7 +576,7 @@ def run_block(args, rank: int, world: int, local_rank: int) -> None:
     rt = _pkg()
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    blk = FluxDoubleBlock(rt, dev)
+    blk = FluxDoubleBlock(rt, dev, fused_norm=not args.unfused_norm)
     g = torch.Generator().manual_seed(100 + rank)
     img = torch.randn(1, 4096, 3072, generator=g).half().to(dev)
     txt = torch.randn(1, 512, 3072, generator=g).half().to(dev)
@@ -608,6 +620,7 @@ def run_block(args, rank: int, world: int, local_rank: int) -> None:
         "data": "synthetic (random-init weights)",
         "config": {"workload": "config4 Flux double block: 4096 img + 512 txt tokens, hidden 3072, 24x128 heads, "
                                "MLP 12288, all linears INT4 W4A8 g128 rot256 perm; attention fp16 SDPA",
+                   "norm": "torch ops" if args.unfused_norm else "LayerNorm + adaLN modulation fused into prep",
                    "parallelism": f"token-sharded x{world} (one sample per GPU, no collective)",
                    "l2": "flushed (256 MB write) between timed steps"},
         "linear_tops": world * lin / (ms * 1e-3) / 1e12, "attn_tflop_per_step": attn / 1e12,
@@ -643,6 +656,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--unfused-norm", action="store_true",
+                    help="flux_block: LayerNorm + modulation as separate torch ops instead of in the prep kernel")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the configs[0] / configs[2] measurements added to the N=1 line")
     ap.add_argument("--workload", choices=["linear", "flux_block"], default="linear",

@@ -106,9 +106,14 @@ def prep_quantize(
     s_a_out: torch.Tensor | None = None,
     x_int8_out: torch.Tensor | None = None,
     x_prep_out: torch.Tensor | None = None,
+    norm: tuple | None = None,
 ):
     """One-pass activation prep (``_ops.py:337-365`` + ``_ops.py:529-533``) and
     per-token INT8 quantisation (``kernels/triton_quantize.py:151-198``).
+
+    ``norm`` = ``("layer", gamma, beta_or_None, eps)`` or ``("rms", gamma,
+    None, eps)`` normalises each row first (fp32 statistics, one rounding to
+    x's dtype), in the same pass (``ic_prep_quant_norm``).
 
     Returns ``(x_int8, s_a, x_prep, rowsum)``; entries not requested are None.
     ``x_int8`` is ``[M, w_in]`` (a view of a buffer whose row stride is w_in
@@ -151,6 +156,22 @@ def prep_quantize(
         rowsum = torch.empty(M, dtype=torch.float32, device=x.device)
     sr = _f32c(smoothrot)
     sm = _f32c(smooth)
+    if norm is not None:
+        kind, gamma, beta, eps = norm
+        code = {"layer": 1, "rms": 2}[kind]
+        if sm is not None:
+            raise ValueError("prep_quantize: a norm with SmoothQuant factors is not supported")
+        g = _f32c(gamma.reshape(-1))
+        b = None if beta is None else _f32c(beta.reshape(-1))
+        if g.numel() != K or (b is not None and b.numel() != K):
+            raise ValueError("prep_quantize: gamma / beta must have K entries")
+        _need_cuda("prep_quantize", g, b)
+        st = L.lib().ic_prep_quant_norm(
+            _p(x2), _DT[x2.dtype], M, K, x2.stride(0), code, _p(g), _p(b), float(eps), _p(sr), int(rot_size), w_in,
+            _p(perm), _p(xq_full), xq_full.stride(0) if xq_full is not None else 0, _p(s_a), _p(x_prep),
+            _p(rowsum), _stream(x2))
+        L.check(st, "ic_prep_quant_norm")
+        return x_int8, s_a, x_prep, rowsum
     st = L.lib().ic_prep_quant(
         _p(x2), _DT[x2.dtype], M, K, x2.stride(0), _p(sr), int(rot_size), w_in, _p(perm), _p(sm),
         _p(xq_full), xq_full.stride(0) if xq_full is not None else 0, _p(s_a), _p(x_prep), _p(rowsum),
@@ -181,6 +202,36 @@ def dynamic_quantize_activation(
         x_int8 = x_int8.reshape(orig)
         s_a = s_a.reshape(orig[:-1])
     return x_int8, s_a
+
+
+def _norm_quantize(x, norm, s_a_out, x_int8_out):
+    orig = x.shape
+    x2 = x.reshape(-1, orig[-1])
+    if s_a_out is not None and s_a_out.shape != (x2.shape[0],):
+        s_a_out = None
+    if x_int8_out is not None and x_int8_out.shape != x2.shape:
+        x_int8_out = None
+    x_int8, s_a, _, _ = prep_quantize(x2, norm=norm, s_a_out=s_a_out, x_int8_out=x_int8_out)
+    if len(orig) > 2:
+        x_int8 = x_int8.reshape(orig)
+        s_a = s_a.reshape(orig[:-1])
+    return x_int8, s_a
+
+
+def fused_layernorm_quantize(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor | None = None,
+                             eps: float = 1e-5, s_a_out: torch.Tensor | None = None,
+                             x_int8_out: torch.Tensor | None = None):
+    """``kernels/triton_quantize.py:274-338``: LayerNorm + per-row INT8 in one
+    pass.  Follows the reference's CPU form: normalised values are cast to
+    x's dtype (fp16/bf16), then quantised half-to-even."""
+    return _norm_quantize(x, ("layer", gamma, beta, eps), s_a_out, x_int8_out)
+
+
+def fused_rmsnorm_quantize(x: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-6,
+                           s_a_out: torch.Tensor | None = None, x_int8_out: torch.Tensor | None = None):
+    """``kernels/triton_quantize.py:395-451``: RMSNorm + per-row INT8 in one pass
+    (CPU form: ``x / sqrt(mean(x^2) + eps) * gamma`` cast to x's dtype)."""
+    return _norm_quantize(x, ("rms", gamma, None, eps), s_a_out, x_int8_out)
 
 
 # ── GEMMs ────────────────────────────────────────────────────────────────────
@@ -484,4 +535,5 @@ __all__ = [
     "dynamic_quantize_activation", "fused_int8_gemm_dequant", "fused_quant_int8_gemm_dequant",
     "fused_w4a8_gemm_dequant", "unpack_int4_to_int8", "unpack_int4_to_float16",
     "prep_quantize", "gemm_a8", "gemm_w4a16", "repack_int4", "lowrank_down", "lowrank_add", "device_error",
+    "fused_layernorm_quantize", "fused_rmsnorm_quantize",
 ]

@@ -40,6 +40,7 @@ SIGNATURES: dict[str, list] = {
     "ic_last_error": [],
     "ic_read_device_error": [_I, ctypes.POINTER(_I)],
     "ic_prep_quant": [_P, _I, _L, _L, _L, _P, _I, _L, _P, _P, _P, _L, _P, _P, _P, _P],
+    "ic_prep_quant_norm": [_P, _I, _L, _L, _L, _I, _P, _P, _F, _P, _I, _L, _P, _P, _L, _P, _P, _P, _P],
     "ic_dynamic_quantize": [_P, _I, _L, _L, _L, _P, _L, _P, _P],
     "ic_gemm_a8": [_P, _L, _L, _L, _P, _I, _L, _L, _P, _L, _L, _P, _P, _I, _P, _P, _P, _I, _L, _P],
     "ic_gemm_a8_splitk": [_P, _L, _L, _L, _P, _I, _L, _L, _P, _L, _L, _P, _P, _I, _P, _P, _P, _I, _L, _I, _P, _L, _P],

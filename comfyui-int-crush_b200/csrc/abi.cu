@@ -68,9 +68,10 @@ int ic_read_device_error(int clear, int* code_out) {
   return IC_OK;
 }
 
-int ic_prep_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const float* smoothrot,
-                  int rot_size, int64_t w_in, const int32_t* perm, const float* smooth, int8_t* x_int8,
-                  int64_t ldq, float* s_a, void* x_prep, float* rowsum, void* stream) {
+static int prep_impl(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int norm, const float* gamma,
+                     const float* beta, float eps, const float* smoothrot, int rot_size, int64_t w_in,
+                     const int32_t* perm, const float* smooth, int8_t* x_int8, int64_t ldq, float* s_a,
+                     void* x_prep, float* rowsum, void* stream) {
   g_err[0] = 0;
   if (x_dtype != IC_DTYPE_F16 && x_dtype != IC_DTYPE_BF16)
     return fail(IC_ERR_ARG, "ic_prep_quant: x dtype must be f16 or bf16");
@@ -90,7 +91,15 @@ int ic_prep_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
   }
   if (!x_int8 && !x_prep && !rowsum) return fail(IC_ERR_ARG, "ic_prep_quant: no output requested");
   if (w_in > 65536 || M > 0x7fffffffLL) return fail(IC_ERR_UNSUPPORTED, "ic_prep_quant: w_in > 65536 or M >= 2^31");
+  if (norm < 0 || norm > 2) return fail(IC_ERR_ARG, "ic_prep_quant_norm: norm must be 0, 1 (layer) or 2 (rms)");
+  if (norm && !gamma) return fail(IC_ERR_ARG, "ic_prep_quant_norm: gamma is required with a norm");
+  if (norm == 2 && beta) return fail(IC_ERR_ARG, "ic_prep_quant_norm: RMSNorm takes no beta");
+  if (norm && smooth) return fail(IC_ERR_UNSUPPORTED, "ic_prep_quant_norm: a norm with SmoothQuant factors is not built");
+  if (norm && rot_size && (rot_size < 16 || rot_size > 256))
+    return fail(IC_ERR_UNSUPPORTED, "ic_prep_quant_norm: with a norm, rot_size must be 0 or in [16, 256]");
   ic::PrepArgs a;
+  memset(&a, 0, sizeof(a));
+  a.norm = norm; a.gamma = gamma; a.beta = beta; a.eps = eps;
   a.x = x; a.M = M; a.K = K; a.ldx = ldx; a.smoothrot = smoothrot; a.w_in = w_in; a.perm = perm;
   a.smooth = smooth; a.xq = x_int8; a.ldq = ldq; a.s_a = s_a; a.x_prep = x_prep; a.rowsum = rowsum;
   a.Kr = Kr; a.Wp = Kr > w_in ? Kr : w_in;
@@ -99,6 +108,21 @@ int ic_prep_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
   const int log2r = rot_size ? ilog2(rot_size) : 0;
   const bool syl = rot_size && !is_pow4(rot_size);
   return cuda_status(ic::launch_prep(a, x_dtype, log2r, syl, (cudaStream_t)stream), "ic_prep_quant launch");
+}
+
+int ic_prep_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const float* smoothrot,
+                  int rot_size, int64_t w_in, const int32_t* perm, const float* smooth, int8_t* x_int8,
+                  int64_t ldq, float* s_a, void* x_prep, float* rowsum, void* stream) {
+  return prep_impl(x, x_dtype, M, K, ldx, 0, nullptr, nullptr, 0.f, smoothrot, rot_size, w_in, perm, smooth,
+                   x_int8, ldq, s_a, x_prep, rowsum, stream);
+}
+
+int ic_prep_quant_norm(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int norm,
+                       const float* gamma, const float* beta, float eps, const float* smoothrot, int rot_size,
+                       int64_t w_in, const int32_t* perm, int8_t* x_int8, int64_t ldq, float* s_a, void* x_prep,
+                       float* rowsum, void* stream) {
+  return prep_impl(x, x_dtype, M, K, ldx, norm, gamma, beta, eps, smoothrot, rot_size, w_in, perm, nullptr,
+                   x_int8, ldq, s_a, x_prep, rowsum, stream);
 }
 
 int ic_dynamic_quantize(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int8_t* x_int8,

@@ -43,6 +43,13 @@ struct PrepArgs {
   int64_t Wp;       // max(Kr, w_in): width of the padded row in shared memory
   double syl_h;     // Sylvester entry (only used for Sylvester sizes)
   int vec_ok;       // 16-byte vector loads of x are legal
+  // optional row normalisation before everything else (prep_row_kernel only):
+  // 0 none, 1 LayerNorm (x - mean) * rstd * gamma + beta, 2 RMSNorm
+  // x / sqrt(mean(x^2) + eps) * gamma; rounded once to the activation dtype
+  int norm;
+  const float* gamma;
+  const float* beta;
+  float eps;
 };
 
 int num_sms();   // gemm_tc.cu
@@ -454,9 +461,10 @@ __device__ __forceinline__ float smoothrot_div(float x, const float* fg, int k, 
 
 template <typename T, int LOG2R, bool SYL, int MAXIT>
 __global__ void __launch_bounds__(kRowThreads) prep_row_kernel(const PrepArgs a, int xr_stride) {
-  static_assert(LOG2R >= 4 && LOG2R <= 8, "prep_row_kernel covers rotation sizes 16..256");
+  static_assert(LOG2R == 0 || (LOG2R >= 4 && LOG2R <= 8), "prep_row_kernel covers no rotation and sizes 16..256");
+  constexpr bool ROT = LOG2R > 0;
   constexpr int R = 1 << LOG2R;
-  constexpr int HB = LOG2R - 4;            // index bits of the second pass
+  constexpr int HB = ROT ? LOG2R - 4 : 0;  // index bits of the second pass
   constexpr int NE = 1 << HB;              // values per second-pass group
   constexpr int GPL = 16 / NE;             // second-pass groups per lane
   extern __shared__ __align__(16) unsigned char smem[];
@@ -468,6 +476,7 @@ __global__ void __launch_bounds__(kRowThreads) prep_row_kernel(const PrepArgs a,
   float* sr = reinterpret_cast<float*>(smem + kRowWarps * kPwBufDoubles * 8 + (size_t)xr_stride * sizeof(T));
   const double scale = SYL ? a.syl_h : 1.0 / (double)(1 << (LOG2R / 2));
   const bool vperm = a.perm && ((w_in & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.perm) & 15) == 0);
+  __shared__ float nred[kRowWarps];
 
   // reciprocals of the SmoothRot factors rounded to the activation dtype
   if (a.smoothrot) {
@@ -475,8 +484,43 @@ __global__ void __launch_bounds__(kRowThreads) prep_row_kernel(const PrepArgs a,
   }
   __syncthreads();
 
+  // fp32 sum of v over the CTA (every thread gets it)
+  auto block_sum_f = [&](float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) nred[warp] = v;
+    __syncthreads();
+    float r = 0.f;
+#pragma unroll
+    for (int w = 0; w < kRowWarps; ++w) r += nred[w];
+    __syncthreads();
+    return r;
+  };
+
   for (int64_t row = blockIdx.x; row < a.M; row += gridDim.x) {
     const T* xrow = reinterpret_cast<const T*>(a.x) + row * a.ldx;
+    // ---- optional normalisation statistics (fp32, two passes for LayerNorm)
+    float mean = 0.f, rstd = 1.f, rms = 1.f;
+    if (a.norm) {
+      float s1 = 0.f;
+      for (int k = threadIdx.x; k < K; k += kRowThreads) {
+        const float f = DT<T>::to_f(xrow[k]);
+        s1 += (a.norm == 1) ? f : f * f;
+      }
+      s1 = block_sum_f(s1);
+      if (a.norm == 1) {
+        mean = s1 / (float)K;
+        float s2 = 0.f;
+        for (int k = threadIdx.x; k < K; k += kRowThreads) {
+          const float d = DT<T>::to_f(xrow[k]) - mean;
+          s2 += d * d;
+        }
+        s2 = block_sum_f(s2);
+        rstd = 1.f / sqrtf(s2 / (float)K + a.eps);
+      } else {
+        rms = sqrtf(s1 / (float)K + a.eps);
+      }
+    }
     // ---- rotation into xr[0, Kr): warp w takes chunks w, w + 8, ...
     for (int c0 = warp * 512; c0 < Kr; c0 += kRowWarps * 512) {
       const int e0 = c0 + 16 * lane;
@@ -499,11 +543,21 @@ __global__ void __launch_bounds__(kRowThreads) prep_row_kernel(const PrepArgs a,
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           float f = DT<T>::to_f(j < 8 ? t0[j] : t1[j - 8]);
+          if (a.norm && e0 + j < K) {
+            const int k = e0 + j;
+            if (a.norm == 1) f = (f - mean) * rstd * __ldg(a.gamma + k) + (a.beta ? __ldg(a.beta + k) : 0.f);
+            else f = f / rms * __ldg(a.gamma + k);
+            f = DT<T>::to_f(DT<T>::from_f(f));
+          }
           if (a.smoothrot && e0 + j < K) f = smoothrot_div<T>(f, a.smoothrot, e0 + j, sr[e0 + j]);
           v[j] = (double)f;
         }
-        butterflies<4, SYL, double>(v);
-        if constexpr (HB == 0) {
+        if constexpr (ROT) butterflies<4, SYL, double>(v);
+        if constexpr (!ROT) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (e0 + j < Kr) xr[e0 + j] = DT<T>::from_d(v[j]);
+        } else if constexpr (HB == 0) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) xr[e0 + j] = DT<T>::from_d(v[j] * scale);
         } else {
@@ -511,7 +565,7 @@ __global__ void __launch_bounds__(kRowThreads) prep_row_kernel(const PrepArgs a,
           for (int j = 0; j < 16; ++j) buf[pidx(16 * lane + j)] = v[j];
         }
       }
-      if constexpr (HB > 0) {
+      if constexpr (ROT && HB > 0) {
         __syncwarp();
 #pragma unroll
         for (int gi = 0; gi < GPL; ++gi) {
@@ -638,10 +692,11 @@ static bool prep_row_fits(const PrepArgs& a, int log2r, size_t tsize) {
   // measured: faster for few rows (4.5 vs 5.7 us for one row); for thousands
   // of rows prep_quant_kernel is faster (68 vs 78 us for 4096 x 3072)
   static const int force_row = [] { const char* e = getenv("INTCRUSH_PREP_ROW"); return (e && e[0] == '1') ? 1 : 0; }();
-  if (log2r < 4 || log2r > 8 || a.smooth || a.M == 0) return false;
+  if (a.smooth || a.M == 0) return false;
+  if (log2r == 0 ? !a.norm : (log2r < 4 || log2r > 8)) return false;
   // many short rows: prep_quant_kernel (68 vs 78 us at 4096 x 3072); few rows
   // or wide rows: this kernel
-  if (a.M >= 4 * num_sms() && a.Wp <= 4096 && !force_row) return false;
+  if (a.M >= 4 * num_sms() && a.Wp <= 4096 && !force_row && !a.norm) return false;
   if ((a.ldq + 1023) / 1024 > 16) return false;
   const size_t smem = (size_t)kRowWarps * kPwBufDoubles * 8 + (size_t)((a.Wp + 15) & ~15LL) * tsize +
                       (a.smoothrot ? (size_t)((a.K + 3) & ~3LL) * sizeof(float) : 0);
@@ -650,6 +705,11 @@ static bool prep_row_fits(const PrepArgs& a, int log2r, size_t tsize) {
 
 template <typename T>
 static cudaError_t launch_prep_dt(const PrepArgs& a, int log2r, bool syl, cudaStream_t st) {
+  if (a.norm) {
+    // row normalisation exists only in prep_row_kernel
+    if (!prep_row_fits(a, log2r, sizeof(T))) return cudaErrorNotSupported;
+    if (log2r == 0) return launch_prep_row<T, 0, false>(a, st);
+  }
   if (log2r == 0) return launch_prep_t<T, 0, false>(a, st);
   if (prep_row_fits(a, log2r, sizeof(T))) {
     if (syl) {

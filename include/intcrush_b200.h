@@ -79,6 +79,22 @@ int ic_prep_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
                   const float* smooth, int8_t* x_int8, int64_t ldq, float* s_a,
                   void* x_prep, float* rowsum, void* stream);
 
+/* ic_prep_quant preceded by a row normalisation, in the same pass:
+ *   norm 1 (LayerNorm): x' = (x - mean) * rstd * gamma + beta (beta may be NULL)
+ *   norm 2 (RMSNorm):   x' = x / sqrt(mean(x^2) + eps) * gamma
+ * with fp32 row statistics, x' rounded once to x's dtype, then SmoothRot,
+ * rotation (rot_size 0 or 16..256), padding, gather and quantisation as in
+ * ic_prep_quant (no SmoothQuant factors).  norm 0 is ic_prep_quant.
+ * Replaces fused_layernorm_quantize / fused_rmsnorm_quantize
+ * (kernels/triton_quantize.py:208-451; rot_size 0, no perm), following their
+ * CPU form (normalised values cast to the activation dtype, then
+ * kernels/triton_quantize.py:43-54), and extends them with the layer's prep.
+ * gamma, beta: fp32 [K]. */
+int ic_prep_quant_norm(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int norm,
+                       const float* gamma, const float* beta, float eps, const float* smoothrot,
+                       int rot_size, int64_t w_in, const int32_t* perm, int8_t* x_int8, int64_t ldq,
+                       float* s_a, void* x_prep, float* rowsum, void* stream);
+
 /* dynamic_quantize_activation (kernels/triton_quantize.py:151-198): the
  * special case of ic_prep_quant with no smoothing, rotation or gather. */
 int ic_dynamic_quantize(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,

@@ -140,6 +140,26 @@ def prep_activation(x16, *, smoothrot=None, rot_need=False, rot_size=0, w_in=Non
     return x
 
 
+def layer_norm_rows(x, gamma, beta=None, eps=1e-5, out_dtype=np.float16) -> np.ndarray:
+    """CPU form of ``fused_layernorm_quantize``'s normalisation
+    (``kernels/triton_quantize.py:316-321``): ``F.layer_norm`` in fp32 (here in
+    fp64, then rounded to fp32), cast to the activation dtype."""
+    xf = np.asarray(x, np.float64)
+    mean = xf.mean(axis=1, keepdims=True)
+    var = ((xf - mean) ** 2).mean(axis=1, keepdims=True)
+    y = (xf - mean) / np.sqrt(var + eps) * np.asarray(gamma, np.float64)
+    if beta is not None:
+        y = y + np.asarray(beta, np.float64)
+    return y.astype(np.float32).astype(out_dtype)
+
+
+def rms_norm_rows(x, gamma, eps=1e-6, out_dtype=np.float16) -> np.ndarray:
+    """CPU form of ``fused_rmsnorm_quantize`` (``kernels/triton_quantize.py:430-435``)."""
+    xf = np.asarray(x, np.float64)
+    rms = np.sqrt((xf * xf).mean(axis=1, keepdims=True) + eps)
+    return (xf / rms * np.asarray(gamma, np.float64)).astype(np.float32).astype(out_dtype)
+
+
 def quantize_rows(x16: np.ndarray):
     """Per-token symmetric INT8 (``kernels/triton_quantize.py:43-54``)."""
     xf = np.asarray(x16).astype(np.float32)

@@ -199,3 +199,32 @@ def test_rotate_activations_cuda_matches_reference_golden():
         y = qu.rotate_activations(x, rot).cpu().numpy().view(np.uint16)
         ref = G[f"rot{rot}_K{K}_y"]
         assert (y != ref).mean() <= 1e-3
+
+
+@pytest.mark.gpu
+def test_flux_block_fused_norm_matches_torch_norm():
+    """The benchmark's DiT block with LayerNorm + adaLN modulation fused into
+    the prep kernel agrees with the same block doing them as torch ops (the
+    two differ only in where fp16 rounding happens)."""
+    import os
+    import sys
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    rt = bench._pkg()
+    dev = torch.device("cuda")
+    kw = dict(hidden=512, heads=4, mlp=1024)
+    fused = bench.FluxDoubleBlock(rt, dev, seed=3, fused_norm=True, **kw)
+    plain = bench.FluxDoubleBlock(rt, dev, seed=3, fused_norm=False, **kw)
+    g = torch.Generator().manual_seed(5)
+    img = torch.randn(1, 96, 512, generator=g).half().to(dev)
+    txt = torch.randn(1, 32, 512, generator=g).half().to(dev)
+    vec = torch.randn(1, 512, generator=g).half().to(dev)
+    with torch.no_grad():
+        a_img, a_txt = fused(img, txt, vec)
+        b_img, b_txt = plain(img, txt, vec)
+    for a, b in ((a_img, b_img), (a_txt, b_txt)):
+        assert torch.isfinite(a).all()
+        err = (a.float() - b.float()).abs().max() / b.float().abs().max()
+        assert err <= 2e-2, float(err)
