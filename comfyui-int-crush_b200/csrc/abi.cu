@@ -270,7 +270,11 @@ int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
   if ((lr_mid == nullptr) != (lr_up == nullptr)) return fail(IC_ERR_ARG, "ic_gemm_w4a16: lr_mid and lr_up go together");
   if (lr_mid && (R <= 0 || R > 64)) return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: low-rank R must be in [1, 64]");
   const cudaStream_t st = (cudaStream_t)stream;
-  if (M <= 32) {
+  static const int skinny_max = [] {
+    const char* e = getenv("INTCRUSH_W4A16_SKINNY_MAX");   // tuning only
+    return e ? atoi(e) : 128;   // measured crossover with the tcgen05 path (3072 x 3072)
+  }();
+  if (M <= skinny_max) {
     ic::SkinnyArgs s;
     s.x = (const __half*)x; s.M = (int)M; s.K = (int)K; s.ldx = ldx; s.w = w; s.N = (int)N; s.ldw = ldw;
     s.scale = scale; s.scale_dtype = scale_dtype; s.G = (int)G; s.group_size = (int)group_size;
@@ -279,7 +283,7 @@ int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
     return cuda_status(ic::launch_w4a16_skinny(s, st), "ic_gemm_w4a16 (small M) launch");
   }
   if (K % 64 || ldx % 8 || !aligned16(x) || ldw % 16 || !aligned16(w))
-    return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: M > 32 needs K %% 64 == 0 and 16-byte aligned rows");
+    return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: M > 128 needs K %% 64 == 0 and 16-byte aligned rows");
   ic::GemmArgs a;
   memset(&a, 0, sizeof(a));
   a.G = (int)G; a.group_size = (int)group_size; a.w_scale = scale; a.w_scale_dtype = scale_dtype;

@@ -1,7 +1,7 @@
 // (a4, a5) Weight-streaming W4A16 for small token counts, the low-rank
 // (LoRA / SVD) down projection and residual, and the INT4 unpack utilities.
 //
-// W4A16 small-M kernel.  For M <= 32 tokens the GEMM is a weight stream:
+// W4A16 small-M kernel.  For M <= 128 tokens (32 per CTA row of the grid) the GEMM is a weight stream:
 // 0.5 byte of HBM per weight against 2*M flops, so the kernel is built to
 // keep the HBM pipe busy, not the tensor pipe.  Weights never touch shared
 // memory: each lane loads 16 packed bytes of two weight rows per 128-k block
@@ -108,6 +108,7 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps, 2) w4a16_skinny_kernel(cons
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int n0 = blockIdx.x * 16;
+  const int m0 = blockIdx.y * 8 * TT;   // token tile (M > 32: one CTA row per 32 tokens)
   const int nkb = (a.K + 127) / 128;
   float d[TT][4];
 #pragma unroll
@@ -139,7 +140,7 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps, 2) w4a16_skinny_kernel(cons
       if (kb >= nkb) break;
       uint32_t xw[TT][16];
 #pragma unroll
-      for (int i = 0; i < TT; ++i) load_x32(a, i * 8 + g, (long long)kb * 128 + 32 * t, xw[i]);
+      for (int i = 0; i < TT; ++i) load_x32(a, m0 + i * 8 + g, (long long)kb * 128 + 32 * t, xw[i]);
       const uint32_t wa[4] = {pa[j].x, pa[j].y, pa[j].z, pa[j].w};
       const uint32_t wb[4] = {pb[j].x, pb[j].y, pb[j].z, pb[j].w};
 #pragma unroll
@@ -177,12 +178,12 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps, 2) w4a16_skinny_kernel(cons
   }
   __syncthreads();
   for (int o = threadIdx.x; o < 16 * 8 * TT; o += blockDim.x) {
-    const int r = o % 16, m = o / 16;   // consecutive threads -> consecutive n
-    const int n = n0 + r;
+    const int r = o % 16, ml = o / 16;   // consecutive threads -> consecutive n
+    const int n = n0 + r, m = m0 + ml;
     if (n >= a.N || m >= a.M) continue;
     float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < kSkinnyWarps; ++w) v += red[w][r][m];
+    for (int w = 0; w < kSkinnyWarps; ++w) v += red[w][r][ml];
     if (a.bias) v += load_any(a.bias, a.bias_dtype, n);
     __half o16 = __float2half_rn(v);
     if (a.lr_mid) {
@@ -197,7 +198,9 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps, 2) w4a16_skinny_kernel(cons
 }
 
 cudaError_t launch_w4a16_skinny(const SkinnyArgs& a, cudaStream_t st) {
-  const dim3 grid((a.N + 15) / 16);
+  // up to 32 tokens per CTA row of the grid; more tokens add CTA rows, each
+  // streaming the (L2-resident) weights again
+  const dim3 grid((a.N + 15) / 16, (a.M + 31) / 32);
   if (a.M <= 8) w4a16_skinny_kernel<1><<<grid, 32 * kSkinnyWarps, 0, st>>>(a);
   else if (a.M <= 16) w4a16_skinny_kernel<2><<<grid, 32 * kSkinnyWarps, 0, st>>>(a);
   else w4a16_skinny_kernel<4><<<grid, 32 * kSkinnyWarps, 0, st>>>(a);
