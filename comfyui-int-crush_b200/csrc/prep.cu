@@ -126,12 +126,27 @@ __device__ __forceinline__ void load16(const PrepArgs& a, const T* xrow, int64_t
     uint4 q0 = __ldg(p), q1 = __ldg(p + 1);
     const T* e0 = reinterpret_cast<const T*>(&q0);
     const T* e1 = reinterpret_cast<const T*>(&q1);
+    // the 16 SmoothRot factors as four 16-byte loads (k0 is a multiple of 16)
+    float srf[16];
+    if (a.smoothrot) {
+      if ((reinterpret_cast<uintptr_t>(a.smoothrot) & 15) == 0) {
+        const float4* sp = reinterpret_cast<const float4*>(a.smoothrot + k0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 f4 = __ldg(sp + i);
+          srf[4 * i] = f4.x; srf[4 * i + 1] = f4.y; srf[4 * i + 2] = f4.z; srf[4 * i + 3] = f4.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) srf[i] = a.smoothrot[k0 + i];
+      }
+    }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       float f0 = DT<T>::to_f(e0[j]), f1 = DT<T>::to_f(e1[j]);
       if (a.smoothrot) {
-        const float s0 = DT<T>::to_f(DT<T>::from_f(a.smoothrot[k0 + j]));
-        const float s1 = DT<T>::to_f(DT<T>::from_f(a.smoothrot[k0 + 8 + j]));
+        const float s0 = DT<T>::to_f(DT<T>::from_f(srf[j]));
+        const float s1 = DT<T>::to_f(DT<T>::from_f(srf[8 + j]));
 #if defined(IC_DIAG_NODIV)   // tuning-only timing variants (wrong results)
         f0 = DT<T>::to_f(DT<T>::from_f(f0 * s0));
         f1 = DT<T>::to_f(DT<T>::from_f(f1 * s1));
