@@ -501,6 +501,16 @@ class _QLinear:
         return y.reshape(*x.shape[:-1], y.shape[-1])
 
 
+def _gather_tokens(t, group):
+    """All-gather [B, heads, L_local, d] along the token axis over the group."""
+    import torch
+    import torch.distributed as dist
+    t = t.contiguous()
+    parts = [torch.empty_like(t) for _ in range(dist.get_world_size(group))]
+    dist.all_gather(parts, t, group=group)
+    return torch.cat(parts, dim=2)
+
+
 class FluxDoubleBlock:
     """Flux-class MMDiT double-stream block: hidden 3072,
     24 heads x 128, MLP 12288 GELU(tanh), adaLN modulation from a 3072-d
@@ -511,24 +521,36 @@ class FluxDoubleBlock:
     With ``fused_norm`` (default) the pre-attention and pre-MLP LayerNorm
     (eps 1e-6, no affine) and the adaLN modulation ``(1 + scale) * x + shift``
     run inside the quantised layer's prep kernel as a LayerNorm with
-    per-sample gamma = 1 + scale, beta = shift (batch 1)."""
+    per-sample gamma = 1 + scale, beta = shift (batch 1).
 
-    def __init__(self, rt, dev, seed=0, hidden=3072, heads=24, mlp=12288, fused_norm=True):
+    With ``sp_group`` (sequence parallel, one sample over the ranks of the
+    group) ``img`` is this rank's contiguous slice of the image tokens and the
+    text tokens are replicated: each rank projects its own tokens, the image
+    tokens' K and V are all-gathered over the group (NCCL), and each rank's
+    queries attend over all keys.  Everything else is token-local, so the
+    per-rank outputs are the matching rows of the single-GPU block.
+    ``linear`` replaces the quantised layer (tests use a CPU stand-in)."""
+
+    def __init__(self, rt, dev, seed=0, hidden=3072, heads=24, mlp=12288, fused_norm=True, sp_group=None,
+                 linear=None, dtype=None):
         import torch
         g = torch.Generator().manual_seed(seed)
         self.fused_norm = fused_norm
+        self.sp_group = sp_group
         self.h, self.nh = hidden, heads
-        mk = lambda o, i: _QLinear(rt, o, i, g, dev)
+        dtype = dtype or torch.float16
+        mk = (lambda o, i: _QLinear(rt, o, i, g, dev)) if linear is None else (lambda o, i: linear(o, i, g))
         self.mod = {s: mk(6 * hidden, hidden) for s in ("img", "txt")}
         self.qkv = {s: mk(3 * hidden, hidden) for s in ("img", "txt")}
         self.proj = {s: mk(hidden, hidden) for s in ("img", "txt")}
         self.fc1 = {s: mk(mlp, hidden) for s in ("img", "txt")}
         self.fc2 = {s: mk(hidden, mlp) for s in ("img", "txt")}
-        self.qn = {s: (1 + 0.1 * torch.randn(128, generator=g)).half().to(dev) for s in ("img", "txt")}
-        self.kn = {s: (1 + 0.1 * torch.randn(128, generator=g)).half().to(dev) for s in ("img", "txt")}
+        self.qn = {s: (1 + 0.1 * torch.randn(128, generator=g)).to(dtype).to(dev) for s in ("img", "txt")}
+        self.kn = {s: (1 + 0.1 * torch.randn(128, generator=g)).to(dtype).to(dev) for s in ("img", "txt")}
+        self.mlp = mlp
 
     def linear_ops(self, n_img: int, n_txt: int) -> float:
-        h, m = self.h, self.fc1["img"].w.shape[0]
+        h, m = self.h, self.mlp
         per_tok = 2 * h * (3 * h + h + m) + 2 * m * h
         return (n_img + n_txt) * per_tok + 2 * 2 * (6 * h) * h
 
@@ -549,6 +571,8 @@ class FluxDoubleBlock:
             q, k, v = qkv.view(B, -1, 3, nh, h // nh).permute(2, 0, 3, 1, 4)
             q = F.rms_norm(q, (h // nh,), self.qn[s])
             k = F.rms_norm(k, (h // nh,), self.kn[s])
+            if s == "img" and self.sp_group is not None:
+                k, v = _gather_tokens(k, self.sp_group), _gather_tokens(v, self.sp_group)
             qs.append(q); ks.append(k); vv.append(v)
         a = F.scaled_dot_product_attention(torch.cat(qs, 2), torch.cat(ks, 2), torch.cat(vv, 2))
         a = a.transpose(1, 2).reshape(B, -1, h)
@@ -576,9 +600,13 @@ def run_block(args, rank: int, world: int, local_rank: int) -> None:
     rt = _pkg()
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    blk = FluxDoubleBlock(rt, dev, fused_norm=not args.unfused_norm)
-    g = torch.Generator().manual_seed(100 + rank)
+    seq = args.shard == "sequence" and world > 1
+    blk = FluxDoubleBlock(rt, dev, fused_norm=not args.unfused_norm, sp_group=dist.group.WORLD if seq else None)
+    g = torch.Generator().manual_seed(100 + (0 if seq else rank))
     img = torch.randn(1, 4096, 3072, generator=g).half().to(dev)
+    if seq:   # one sample over all ranks: this rank's image tokens
+        per = 4096 // world
+        img = img[:, rank * per:(rank + 1) * per].contiguous()
     txt = torch.randn(1, 512, 3072, generator=g).half().to(dev)
     vec = torch.randn(1, 3072, generator=g).half().to(dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
@@ -614,16 +642,18 @@ def run_block(args, rank: int, world: int, local_rank: int) -> None:
     lin = blk.linear_ops(4096, 512)
     attn = 4 * n_tok * n_tok * 3072
     line = {
-        "metric": "flux_double_block_tokens_per_s", "value": world * n_tok / (ms * 1e-3), "unit": "tokens/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8+fp16",
+        "metric": "flux_double_block_tokens_per_s", "value": (1 if seq else world) * n_tok / (ms * 1e-3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong" if seq else "weak", "vs_baseline": None, "dtype": "int8+fp16",
         "data": "synthetic (random-init weights)",
         "config": {"workload": "config4 Flux double block: 4096 img + 512 txt tokens, hidden 3072, 24x128 heads, "
                                "MLP 12288, all linears INT4 W4A8 g128 rot256 perm; attention fp16 SDPA",
                    "norm": "torch ops" if args.unfused_norm else "LayerNorm + adaLN modulation fused into prep",
-                   "parallelism": f"token-sharded x{world} (one sample per GPU, no collective)",
+                   "parallelism": (f"sequence-parallel x{world}: one sample, image tokens split, text replicated, "
+                                   "K/V all-gather (NCCL)") if seq else
+                                  f"token-sharded x{world} (one sample per GPU, no collective)",
                    "l2": "flushed (256 MB write) between timed steps"},
-        "linear_tops": world * lin / (ms * 1e-3) / 1e12, "attn_tflop_per_step": attn / 1e12,
+        "linear_tops": (1 if seq else world) * lin / (ms * 1e-3) / 1e12, "attn_tflop_per_step": attn / 1e12,
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
@@ -662,9 +692,10 @@ def main():
                     help="skip the configs[0] / configs[2] measurements added to the N=1 line")
     ap.add_argument("--workload", choices=["linear", "flux_block"], default="linear",
                     help="linear: BASELINE configs[1] (default); flux_block: configs[3]")
-    ap.add_argument("--shard", choices=["tokens", "features"], default="tokens",
-                    help="tokens: every rank runs its own 4096 tokens (default); "
-                         "features: one layer split by output features + all-gather")
+    ap.add_argument("--shard", choices=["tokens", "features", "sequence"], default="tokens",
+                    help="tokens: every rank runs its own tokens / sample (default); "
+                         "features: one layer split by output features + all-gather; "
+                         "sequence (flux_block): one sample split by image tokens + K/V all-gather")
     ap.add_argument("--kernel-probe", choices=["prep", "gemm"], default=None,
                     help="run only this kernel of the step (3 launches) for profiling; prints nothing")
     args = ap.parse_args()

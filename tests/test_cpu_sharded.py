@@ -4,7 +4,10 @@ The GEMM itself is CUDA-only, so these tests give ``FeatureShardedLinear``
 CPU stand-ins for the prep and GEMM callables (the numpy oracle) and check
 the sharding logic: which weight rows each rank keeps, the padding of the
 last rank, the all-gather and the column order of the assembled output, and
-that the assembled output equals the single-process forward exactly.
+that the assembled output equals the single-process forward exactly.  The
+last test runs the benchmark's DiT block sequence-parallel (one sample split
+by image tokens, K/V all-gathered) with CPU stand-ins for the linears and
+compares it with the single-process block.
 """
 
 import os
@@ -111,3 +114,67 @@ def test_shard_tokens_cover_once():
     x = torch.arange(11 * 3).reshape(11, 3)
     parts = [sh.shard_tokens(x, r, 4) for r in range(4)]
     assert torch.equal(torch.cat(parts), x)
+
+
+class _TorchLinear:
+    """CPU stand-in for the quantised layer of the benchmark's DiT block."""
+
+    def __init__(self, n_out, n_in, g):
+        self.w = torch.randn(n_out, n_in, generator=g) / n_in ** 0.5
+        self.b = torch.randn(n_out, generator=g) * 0.02
+
+    def __call__(self, x, norm=None):
+        if norm is not None:
+            _, gamma, beta, eps = norm
+            x = torch.nn.functional.layer_norm(x, (x.shape[-1],), eps=eps) * gamma + beta
+        return x @ self.w.T + self.b
+
+
+def _block(sp_group):
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    return bench.FluxDoubleBlock(None, torch.device("cpu"), seed=4, hidden=256, heads=2, mlp=512,
+                                 sp_group=sp_group, linear=_TorchLinear, dtype=torch.float32)
+
+
+def _block_inputs():
+    g = torch.Generator().manual_seed(8)
+    return (torch.randn(1, 64, 256, generator=g), torch.randn(1, 16, 256, generator=g),
+            torch.randn(1, 256, generator=g))
+
+
+def _sp_worker(rank, world, port, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        img, txt, vec = _block_inputs()
+        per = img.shape[1] // world
+        blk = _block(dist.group.WORLD)
+        with torch.no_grad():
+            o_img, o_txt = blk(img[:, rank * per:(rank + 1) * per].contiguous(), txt, vec)
+        out_q.put((rank, o_img.numpy(), o_txt.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sequence_parallel_block_matches_single_process():
+    """One sample split by image tokens over 2 gloo ranks (K/V all-gather)
+    gives the rows of the single-process block."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sp_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=180) for _ in range(world)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    img, txt, vec = _block_inputs()
+    with torch.no_grad():
+        r_img, r_txt = _block(None)(img, txt, vec)
+    got = np.concatenate([r[1] for r in res], axis=1)
+    np.testing.assert_allclose(got, r_img.numpy(), rtol=1e-4, atol=1e-4)
+    for r in res:
+        np.testing.assert_allclose(r[2], r_txt.numpy(), rtol=1e-4, atol=1e-4)
