@@ -590,6 +590,151 @@ class FluxDoubleBlock:
         return outs[1], outs[0]
 
 
+class _QLinear8:
+    """INT8 W8A8 linear with per-channel scales and rot 1024 (BASELINE
+    configs[4]), through the runtime's fused prep and GEMM (random-init)."""
+
+    def __init__(self, rt, n_out: int, n_in: int, g, dev, rot: int = 1024):
+        import torch
+        self.rt, self.rot, self.n_in = rt, rot, n_in
+        # rotated layers store weights for the padded width (13824 -> 14336), zero past K
+        n_in_p = -(-n_in // rot) * rot
+        w = torch.zeros(n_out, n_in_p, dtype=torch.int8)
+        w[:, :n_in] = torch.randint(-127, 128, (n_out, n_in), generator=g, dtype=torch.int8)
+        self.w = w.to(dev)
+        self.s = (torch.rand(n_out, generator=g) * 1e-4 + 2e-5).float().to(dev)
+        self.b = (torch.randn(n_out, generator=g) * 0.02).half().to(dev)
+
+    def __call__(self, x):
+        x2 = x.reshape(-1, x.shape[-1])
+        xq, s_a, _, _ = self.rt.prep_quantize(x2, rot_size=self.rot)
+        y = self.rt.gemm_a8(xq, self.w, self.s, s_a, bias=self.b, out_dtype=x.dtype)
+        return y.reshape(*x.shape[:-1], y.shape[-1])
+
+
+class WanBlock:
+    """Wan-class DiT block: hidden 5120, 40 heads x 128,
+    self-attention with q/k RMSNorm, cross-attention to 512 text tokens, FFN
+    13824 GELU(tanh), adaLN-style modulation (shift/scale/gate for attention
+    and FFN, one 6 x 5120 vector per sample, random), all linears W8A8
+    per-channel with rot 1024.  Norms, modulation, GELU and attention (torch
+    SDPA) run in fp16.  ``sp_group``: the sample's tokens are split over the
+    group and self-attention K/V are all-gathered (as in FluxDoubleBlock)."""
+
+    def __init__(self, rt, dev, seed=0, hidden=5120, heads=40, ffn=13824, sp_group=None):
+        import torch
+        g = torch.Generator().manual_seed(seed)
+        self.h, self.nh, self.sp_group = hidden, heads, sp_group
+        mk = lambda o, i: _QLinear8(rt, o, i, g, dev)
+        self.q, self.k, self.v, self.o = (mk(hidden, hidden) for _ in range(4))
+        self.cq, self.ck, self.cv, self.co = (mk(hidden, hidden) for _ in range(4))
+        self.fc1, self.fc2 = mk(ffn, hidden), mk(hidden, ffn)
+        self.qn = (1 + 0.1 * torch.randn(hidden, generator=g)).half().to(dev)
+        self.kn = (1 + 0.1 * torch.randn(hidden, generator=g)).half().to(dev)
+        self.n3 = (1 + 0.1 * torch.randn(hidden, generator=g)).half().to(dev)
+        self.ffn = ffn
+
+    def linear_ops(self, n_tok: int, n_ctx: int) -> float:
+        h = self.h
+        return 2 * n_tok * (6 * h * h + 2 * h * self.ffn) + 2 * n_ctx * 2 * h * h
+
+    def __call__(self, x, ctx, mod):
+        import torch
+        import torch.nn.functional as F
+        B, L, h = x.shape
+        nh, hd = self.nh, h // self.nh
+        sh1, sc1, g1, sh2, sc2, g2 = mod.chunk(6, dim=1)          # [B, 1, h] each
+        y = F.layer_norm(x, (h,), eps=1e-6) * (1 + sc1) + sh1
+        q = F.rms_norm(self.q(y), (h,), self.qn, eps=1e-6).view(B, L, nh, hd).transpose(1, 2)
+        k = F.rms_norm(self.k(y), (h,), self.kn, eps=1e-6).view(B, L, nh, hd).transpose(1, 2)
+        v = self.v(y).view(B, L, nh, hd).transpose(1, 2)
+        if self.sp_group is not None:
+            k, v = _gather_tokens(k, self.sp_group), _gather_tokens(v, self.sp_group)
+        a = F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(B, L, h)
+        x = x + g1 * self.o(a)
+        y = F.layer_norm(x, (h,), self.n3, eps=1e-6)
+        Lc = ctx.shape[1]
+        cq = self.cq(y).view(B, L, nh, hd).transpose(1, 2)
+        ck = self.ck(ctx).view(B, Lc, nh, hd).transpose(1, 2)
+        cv = self.cv(ctx).view(B, Lc, nh, hd).transpose(1, 2)
+        a = F.scaled_dot_product_attention(cq, ck, cv).transpose(1, 2).reshape(B, L, h)
+        x = x + self.co(a)
+        y = F.layer_norm(x, (h,), eps=1e-6) * (1 + sc2) + sh2
+        return x + g2 * self.fc2(F.gelu(self.fc1(y), approximate="tanh"))
+
+
+def run_wan(args, rank: int, world: int, local_rank: int) -> None:
+    """a stack of 8 Wan-class blocks, batch 2 x 32760
+    video tokens, 512 text-context tokens (not specified by BASELINE; stated).
+    Weak layout (default): every rank runs the whole batch-2 stack (or its
+    share of the batch when world divides 2); sequence layout: the tokens of
+    each sample are split over the ranks with a K/V all-gather per block.
+    tokens/s = processed tokens / max-over-ranks stack time."""
+    import torch
+    import torch.distributed as dist
+    rt = _pkg()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    seq = args.shard == "sequence" and world > 1
+    L, B, n_ctx = args.wan_tokens, 2, 512
+    blocks = [WanBlock(rt, dev, seed=10 + i, sp_group=dist.group.WORLD if seq else None) for i in range(args.wan_blocks)]
+    g = torch.Generator().manual_seed(200 + (0 if seq else rank))
+    x = torch.randn(B, L, 5120, generator=g).half()
+    if seq:
+        per = L // world
+        x = x[:, rank * per:(rank + 1) * per]
+    x = x.contiguous().to(dev)
+    ctx = (torch.randn(B, n_ctx, 5120, generator=g) * 0.5).half().to(dev)
+    mod = (torch.randn(B, 6, 5120, generator=g) * 0.1).half().to(dev)
+    st = torch.cuda.current_stream()
+
+    def stack(t):
+        for blk in blocks:
+            t = blk(t, ctx, mod)
+        return t
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            stack(x)
+        torch.cuda.synchronize()
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        with Clocks(local_rank) as clk:
+            _gpu_head_start()
+            for i in range(args.steps):
+                ev[i][0].record(st)
+                stack(x)
+                ev[i][1].record(st)
+            torch.cuda.synchronize()
+    tot = sum(e[0].elapsed_time(e[1]) for e in ev)
+    vals = torch.tensor([tot], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    if rank != 0:
+        return
+    ms = vals.item() / args.steps
+    toks = B * L * (1 if seq else world)
+    lin_rank = blocks[0].linear_ops(B * x.shape[1], B * n_ctx) * len(blocks)   # this rank's linear work
+    line = {
+        "metric": "wan_stack_tokens_per_s", "value": toks / (ms * 1e-3), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong" if seq else "weak", "vs_baseline": None,
+        "dtype": "int8+fp16", "data": "synthetic (random-init weights)",
+        "config": {"workload": f"config5 Wan stack: {len(blocks)} blocks, batch 2 x {L} tokens, hidden 5120, "
+                               "40x128 heads, FFN 13824, W8A8 per-channel rot 1024; 512 text-context tokens "
+                               "(not specified by BASELINE); attention fp16 SDPA",
+                   "parallelism": (f"sequence-parallel x{world} (K/V all-gather)" if seq else
+                                   f"token-sharded x{world} (whole batch per GPU, no collective)"),
+                   "l2": "inputs far larger than L2"},
+        "linear_tops": world * lin_rank / (ms * 1e-3) / 1e12,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_block(args, rank: int, world: int, local_rank: int) -> None:
     """one Flux-class double block, 4096 image + 512
     text tokens, batch 1 per GPU (token sharding across GPUs: each rank runs
@@ -690,8 +835,10 @@ def main():
                     help="flux_block: LayerNorm + modulation as separate torch ops instead of in the prep kernel")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the configs[0] / configs[2] measurements added to the N=1 line")
-    ap.add_argument("--workload", choices=["linear", "flux_block"], default="linear",
-                    help="linear: BASELINE configs[1] (default); flux_block: configs[3]")
+    ap.add_argument("--workload", choices=["linear", "flux_block", "wan_stack"], default="linear",
+                    help="linear: BASELINE configs[1] (default); flux_block: configs[3]; wan_stack: configs[4]")
+    ap.add_argument("--wan-tokens", type=int, default=32760, help="wan_stack: tokens per sample")
+    ap.add_argument("--wan-blocks", type=int, default=8, help="wan_stack: blocks in the stack")
     ap.add_argument("--shard", choices=["tokens", "features", "sequence"], default="tokens",
                     help="tokens: every rank runs its own tokens / sample (default); "
                          "features: one layer split by output features + all-gather; "
@@ -717,6 +864,8 @@ def main():
     try:
         if args.workload == "flux_block":
             run_block(args, rank, world, local_rank)
+        elif args.workload == "wan_stack":
+            run_wan(args, rank, world, local_rank)
         else:
             (run_features if args.shard == "features" else run_gpu)(args, rank, world, local_rank)
     finally:
