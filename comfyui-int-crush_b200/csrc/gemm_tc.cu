@@ -70,7 +70,22 @@ struct GemmArgs {
   int splits;
   int kb_per_unit;
   float* ws;
+  int group_m;      // tile order: all weight tiles of group_m consecutive token tiles, then the next group
 };
+
+// Tile index -> (weight tile, token tile).  Tiles run in groups of group_m
+// token tiles; within a group the token tile varies fastest.  A wave of CTAs
+// then covers a few token tiles x many weight tiles, so both operands of the
+// wave stay in L2 when the activations do not fit in it (large M).
+__device__ __forceinline__ void tile_nm(const GemmArgs& a, int tile, int& n_blk, int& m_blk) {
+  const int per_group = a.group_m * a.n_tiles;
+  const int grp = tile / per_group;
+  const int first_m = grp * a.group_m;
+  const int gsz = min(a.group_m, a.m_tiles - first_m);
+  const int r = tile - grp * per_group;
+  m_blk = first_m + r % gsz;
+  n_blk = r / gsz;
+}
 
 constexpr int kTileN = 128;            // weight rows per tile (UMMA M)
 constexpr uint32_t kMagic = 0x4B400000u;
@@ -359,7 +374,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       bool ok = true;
       for (int wu = blockIdx.x; ok && wu < total_units; wu += gridDim.x) {
         const int tile = wu / a.splits, kb_lo = (wu % a.splits) * a.kb_per_unit;
-        const int n_blk = tile / a.m_tiles, m_blk = tile % a.m_tiles;
+        int n_blk, m_blk;
+        tile_nm(a, tile, n_blk, m_blk);
         for (int kb = kb_lo; kb < kb_lo + a.kb_per_unit; ++kb, ++it) {
           const int s = it % SX;
           const uint32_t ph = (uint32_t)(it / SX) & 1u;
@@ -447,7 +463,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         const int wu_j = blockIdx.x + (j / a.kb_per_unit) * gridDim.x;
         if (wu_j >= total_units) return;
         const int kb = (wu_j % a.splits) * a.kb_per_unit + j % a.kb_per_unit;
-        const int n_blk = (wu_j / a.splits) / a.m_tiles;
+        int n_blk, m_unused;
+        tile_nm(a, wu_j / a.splits, n_blk, m_unused);
         const int sp = j % SP;
         mbar_arrive_expect_tx(&p_full[sp], (uint32_t)C::P_BYTES);
         tma_load_2d(p_stage(sp), &tm_w, &p_full[sp], kb * (MODE == W_I4 ? 64 : 32), n_blk * kTileN);
@@ -459,7 +476,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       bool ok = true;
       const bool rp = a.w_repacked != 0;
       for (int wu = blockIdx.x; ok && wu < total_units; wu += gridDim.x) {
-        const int n_blk = (wu / a.splits) / a.m_tiles, kb_lo = (wu % a.splits) * a.kb_per_unit;
+        int n_blk, m_unused;
+        tile_nm(a, wu / a.splits, n_blk, m_unused);
+        const int kb_lo = (wu % a.splits) * a.kb_per_unit;
         for (int kb = kb_lo; kb < kb_lo + a.kb_per_unit; ++kb, ++it) {
           if ((it & 1) != xw) continue;
           const int sp = it % SP, sw = it % SW;
@@ -594,7 +613,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     bool ok = true;
     for (int wu = blockIdx.x; ok && wu < total_units; wu += gridDim.x) {
       const int tile = wu / a.splits, split = wu % a.splits;
-      const int n_blk = tile / a.m_tiles, m_blk = tile % a.m_tiles;
+      int n_blk, m_blk;
+      tile_nm(a, tile, n_blk, m_blk);
       const int n = n_blk * kTileN + 32 * q + lane;
       const bool nvalid = n < a.N;
       const float bias_n = (nvalid && a.bias) ? load_any(a.bias, a.bias_dtype, n) : 0.f;
@@ -782,6 +802,11 @@ template <int MODE, bool GROUPED>
 static cudaError_t dispatch_bn(int bn, const CUtensorMap& tw, const CUtensorMap& tx, GemmArgs a,
                                cudaStream_t st) {
   a.m_tiles = (a.M + bn - 1) / bn;
+  {
+    static const int gm_env = [] { const char* e = getenv("INTCRUSH_GROUP_M"); return e ? atoi(e) : 0; }();
+    const int gm = gm_env > 0 ? gm_env : 16;
+    a.group_m = gm < a.m_tiles ? gm : a.m_tiles;
+  }
   switch (bn) {
     case 32: return launch_gemm_t<MODE, 32, GROUPED>(tw, tx, a, st);
     case 64: return launch_gemm_t<MODE, 64, GROUPED>(tw, tx, a, st);
