@@ -496,7 +496,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
           uint8_t* W = w_stage(sw);
           const uint8_t* P = p_stage(sp);
-#if !defined(IC_DIAG_NOEXPAND)   // tuning-only: measure the pipeline without the expansion work
           if constexpr (MODE == W_I4) {
             // all sixteen 16-byte loads first: one shared-memory latency per
             // stage instead of one per few rows
@@ -577,7 +576,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
               }
             }
           }
-#endif
 #if defined(IC_TRACE)
           __syncwarp();
           if (lane == 0) IC_TADD(7);

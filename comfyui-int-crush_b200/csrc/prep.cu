@@ -147,13 +147,8 @@ __device__ __forceinline__ void load16(const PrepArgs& a, const T* xrow, int64_t
       if (a.smoothrot) {
         const float s0 = DT<T>::to_f(DT<T>::from_f(srf[j]));
         const float s1 = DT<T>::to_f(DT<T>::from_f(srf[8 + j]));
-#if defined(IC_DIAG_NODIV)   // tuning-only timing variants (wrong results)
-        f0 = DT<T>::to_f(DT<T>::from_f(f0 * s0));
-        f1 = DT<T>::to_f(DT<T>::from_f(f1 * s1));
-#else
         f0 = DT<T>::to_f(DT<T>::from_f(__fdiv_rn(f0, s0)));
         f1 = DT<T>::to_f(DT<T>::from_f(__fdiv_rn(f1, s1)));
-#endif
       }
       v[j] = to_rot<V, T>(f0);
       v[8 + j] = to_rot<V, T>(f1);
@@ -226,12 +221,8 @@ __device__ __forceinline__ void rot_pass(const PrepArgs& a, const T* xrow, int c
 #pragma unroll
       for (int j = 0; j < E; ++j) {
         T out;
-#if defined(IC_DIAG_NOD2H)
-        out = DT<T>::from_f((float)(v[j] * (1.0 / (double)(1 << (LOG2R / 2)))));
-#else
         if constexpr (SYL) out = DT<T>::from_d(v[j] * a.syl_h);
         else out = DT<T>::from_d(v[j] * (1.0 / (double)(1 << (LOG2R / 2))));   // 2^-D, exact
-#endif
         xr[c0 + base + (j << S)] = out;
       }
     } else {
@@ -373,9 +364,7 @@ __global__ void __launch_bounds__(NT) prep_quant_kernel(const PrepArgs a) {
             const float xv = DT<T>::to_f(xp[j]);
             float y = xv * rs;
             const float fy = fabsf(y);
-#if !defined(IC_DIAG_NOQCHK)
             if (fabsf(fy - (floorf(fy) + 0.5f)) <= fy * 4.8e-7f) y = __fdiv_rn(xv, s);
-#endif
             q = max(-128, min(127, __float_as_int(y + 12582912.0f) - 0x4B400000));
           }
           word |= ((uint32_t)(q & 0xFF)) << (8 * b);
