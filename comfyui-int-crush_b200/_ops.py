@@ -194,8 +194,9 @@ def make_intcrush_ops(quant_format: str, rot_size: int, use_pytorch: bool = Fals
                 return bw
 
             def _repacked(self, bw: _B200Weights, qdata: torch.Tensor, layout: int):
-                """Nibble-repacked INT4 copy for the GEMMs (opt-in: it costs a
-                second copy of the INT4 weights; INTCRUSH_REPACK=1)."""
+                """Nibble-repacked INT4 copy for the GEMMs (on by default; it
+                costs a second copy of the INT4 weights, INTCRUSH_REPACK=0 turns
+                it off)."""
                 if not _REPACK:
                     return None
                 attr = "rep_a8" if layout == 0 else "rep_a16"
@@ -609,8 +610,9 @@ def make_intcrush_ops(quant_format: str, rot_size: int, use_pytorch: bool = Fals
 import os as _os
 
 # Keep a nibble-repacked copy of INT4 weights for the GEMMs (faster INT4
-# expansion, costs one extra copy of the INT4 weights).  INTCRUSH_REPACK=1.
-_REPACK = _os.environ.get("INTCRUSH_REPACK", "0") == "1"
+# expansion, costs one extra copy of the INT4 weights).  On by default;
+# INTCRUSH_REPACK=0 keeps only the reference packing.
+_REPACK = _os.environ.get("INTCRUSH_REPACK", "1") == "1"
 
 
 def _round_to(t: torch.Tensor | None, dtype: torch.dtype) -> torch.Tensor | None:

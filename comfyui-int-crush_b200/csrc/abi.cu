@@ -155,6 +155,14 @@ static int gemm_a8_impl(const char* fn, const int8_t* xq, int64_t M, int64_t K, 
     if ((K + group_size - 1) / group_size != G) return fail(IC_ERR_ARG, "%s: G != ceil(K / group_size)", fn);
     if (w_kind == IC_W_INT8 && group_size > 128)
       return fail(IC_ERR_UNSUPPORTED, "%s: int8 weights with group scales need group_size == 128", fn);
+    // INT4 is held as 16*q inside the kernel; a group's int32 partial is then
+    // at most 2^22 in magnitude for 256-wide groups, the limit of the exact
+    // int -> float hand-off (1.5*2^23 + P must keep its exponent).
+    if (w_kind != IC_W_INT8 && group_size > 256)
+      return fail(IC_ERR_UNSUPPORTED, "%s: int4 weights with group scales need group_size 128 or 256", fn);
+    // every group must span whole 128-wide K blocks, the last one included
+    if (((K + 127) / 128) % (group_size / 128) != 0)
+      return fail(IC_ERR_UNSUPPORTED, "%s: ceil(K / 128) must be a multiple of group_size / 128", fn);
   }
   if (M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL) return fail(IC_ERR_UNSUPPORTED, "%s: dims >= 2^31", fn);
   ic::GemmArgs a;
@@ -169,7 +177,9 @@ static int gemm_a8_impl(const char* fn, const int8_t* xq, int64_t M, int64_t K, 
     if (nkb % splits) return fail(IC_ERR_ARG, "%s: ceil(K / 128) must be a multiple of splits", fn);
     if (G > 1 && (K % group_size || G % splits))
       return fail(IC_ERR_ARG, "%s: with group scales, K %% group_size == 0 and G %% splits == 0", fn);
-    if (!ws || ws_elems < (int64_t)splits * M * N) return fail(IC_ERR_ARG, "%s: workspace needs splits*M*N floats", fn);
+    // M, N < 2^31 and splits <= 16 here: the product fits in 128 bits
+    if (!ws || (__int128)ws_elems < (__int128)splits * M * N)
+      return fail(IC_ERR_ARG, "%s: workspace needs splits*M*N floats", fn);
   }
   a.splits = splits;
   a.ws = ws;
@@ -211,24 +221,51 @@ static __device__ __align__(256) float g_splitk_scratch[IC_NOALLOC_SCRATCH_FLOAT
 
 namespace {
 std::mutex g_scratch_mu;
-float* g_scratch_ptr[64] = {nullptr};   // device address of g_splitk_scratch, per device
+// Device address of g_splitk_scratch per CUDA context.  An address is valid
+// only in the context that produced it, so the cache is keyed on the current
+// context (cuCtxGetCurrent, fetched through the runtime so that the library
+// does not link libcuda), not on the device index: a host that drives the
+// device through its own driver-API context, or that reset the device, gets
+// the address of its own context.
+struct ScratchEntry { void* ctx; float* ptr; };
+ScratchEntry g_scratch[64];
+int g_scratch_used = 0;
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
 }  // namespace
 
+static void* current_context() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (CtxGetCurrentFn) nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  CUcontext c = nullptr;
+  if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return (void*)c;
+}
+
 // Host code sees g_splitk_scratch only as a host-side stand-in: its device
-// address is asked for once per device, with that device current.
+// address is asked for once per context, with the caller's device current.
 static int scratch_for_current_device(const char* fn, float** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
-  if (dev < 0 || dev >= 64) return fail(IC_ERR_UNSUPPORTED, "%s: device index %d >= 64", fn, dev);
+  (void)dev;
+  void* ctx = current_context();
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_splitk_scratch);
-    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress of the split-K scratch");
-    g_scratch_ptr[dev] = static_cast<float*>(p);
-  }
-  *out = g_scratch_ptr[dev];
+  for (int i = 0; ctx && i < g_scratch_used; ++i)
+    if (g_scratch[i].ctx == ctx) { *out = g_scratch[i].ptr; return IC_OK; }
+  // first call in this context (the runtime makes the device's primary
+  // context current here if nothing was current yet)
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_splitk_scratch);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress of the split-K scratch");
+  if (!ctx) ctx = current_context();
+  if (ctx && g_scratch_used < 64) g_scratch[g_scratch_used++] = ScratchEntry{ctx, static_cast<float*>(p)};
+  *out = static_cast<float*>(p);
   return IC_OK;
 }
 
@@ -240,9 +277,10 @@ int ic_gemm_a8_splitk_noalloc(const int8_t* xq, int64_t M, int64_t K, int64_t ld
   const char* fn = "ic_gemm_a8_splitk_noalloc";
   g_err[0] = 0;
   if (M < 0 || N < 0 || splits < 1 || splits > 16) return fail(IC_ERR_ARG, "%s: bad M/N/splits", fn);
-  if (splits > 1 && (int64_t)splits * M * N > (int64_t)IC_NOALLOC_SCRATCH_FLOATS)
-    return fail(IC_ERR_ARG, "%s: splits*M*N = %lld exceeds the built-in scratch of %lld floats", fn,
-                (long long)splits * M * N, (long long)IC_NOALLOC_SCRATCH_FLOATS);
+  // compared without forming splits * M * N first (it could overflow int64)
+  if (splits > 1 && N > 0 && M > (int64_t)IC_NOALLOC_SCRATCH_FLOATS / splits / N)
+    return fail(IC_ERR_ARG, "%s: splits*M*N (%d * %lld * %lld) exceeds the built-in scratch of %lld floats", fn,
+                splits, (long long)M, (long long)N, (long long)IC_NOALLOC_SCRATCH_FLOATS);
   float* ws = nullptr;
   if (splits > 1 && M > 0 && N > 0) {
     const int st = scratch_for_current_device(fn, &ws);

@@ -156,8 +156,9 @@ int ic_gemm_a8_splitk(const int8_t* xq, int64_t M, int64_t K, int64_t ldq,
  * into the library (IC_NOALLOC_SCRATCH_FLOATS floats = 8 MiB, held on every
  * GPU that loads the library until the process exits); calls that would need
  * more (splits * M * N floats) are rejected with IC_ERR_ARG before any work is
- * queued.  The first call on a device looks up the scratch address for that
- * device (cudaGetSymbolAddress, with the device current); make that first call
+ * queued.  The first call in a CUDA context (normally the device's primary
+ * context) looks up the scratch address for that context
+ * (cudaGetSymbolAddress, with the device current); make that first call
  * before any stream capture.  Every call shares the one array and the GEMM
  * overwrites every element the reduce reads, so nothing needs clearing, but
  * calls whose GPU work overlaps (different streams, or different host threads

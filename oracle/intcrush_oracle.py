@@ -100,43 +100,61 @@ def f16(a) -> np.ndarray:
     return np.asarray(a, dtype=np.float64).astype(np.float16)
 
 
-def div_f16(x16: np.ndarray, d) -> np.ndarray:
-    """fp16 tensor divided by a vector cast to fp16, as ``x / f.to(x.dtype)``:
-    the quotient is correctly rounded to fp16 (fp64 then fp16 is a safe
-    double rounding for division)."""
-    d16 = np.asarray(d, dtype=np.float32).astype(np.float16)
-    return (x16.astype(np.float64) / d16.astype(np.float64)).astype(np.float16)
+def bf16(a) -> np.ndarray:
+    """Round to bfloat16 (nearest, ties to even) directly from float64, returned
+    as float32 values (numpy has no bfloat16 dtype).  bf16 keeps 8 significant
+    bits; frexp's mantissa in [0.5, 1) times 2^8 is rounded half-even by rint.
+    Subnormal and overflowing values are outside what the tests feed it."""
+    x = np.asarray(a, dtype=np.float64)
+    m, e = np.frexp(x)
+    return np.ldexp(np.rint(np.ldexp(m, 8)), e - 8).astype(np.float32)
 
 
-def rotate(x16: np.ndarray, rot_size: int) -> np.ndarray:
+def round_act(a, act: str = "f16") -> np.ndarray:
+    """Round float64 values to the activation dtype: fp16 (as float16) or
+    bf16 (as float32 holding bf16 values)."""
+    return f16(a) if act == "f16" else bf16(a)
+
+
+def div_f16(x16: np.ndarray, d, act: str = "f16") -> np.ndarray:
+    """Activation tensor divided by a vector cast to the activation dtype, as
+    ``x / f.to(x.dtype)``: the quotient is correctly rounded to that dtype
+    (fp64 then fp16/bf16 is a safe double rounding for division)."""
+    d_act = round_act(np.asarray(d, dtype=np.float32), act)
+    return round_act(np.asarray(x16, np.float64) / np.asarray(d_act, np.float64), act)
+
+
+def rotate(x16: np.ndarray, rot_size: int, act: str = "f16") -> np.ndarray:
     """``rotate_activations`` (``_quant_utils.py:117-147``) with an exact sum."""
     if not is_power_of_two(rot_size):
         raise ValueError(f"rot_size must be power of 2, got {rot_size}")
     M, K = x16.shape
     Kp = -(-K // rot_size) * rot_size
     xp = np.zeros((M, Kp), dtype=np.float64)
-    xp[:, :K] = x16.astype(np.float64)
+    xp[:, :K] = np.asarray(x16, np.float64)
     H = hadamard(rot_size)
     y = xp.reshape(M, Kp // rot_size, rot_size) @ H.T
-    return y.reshape(M, Kp).astype(np.float16)
+    return round_act(y.reshape(M, Kp), act)
 
 
 def prep_activation(x16, *, smoothrot=None, rot_need=False, rot_size=0, w_in=None,
-                    perm=None, smooth=None, int8_path=True) -> np.ndarray:
+                    perm=None, smooth=None, int8_path=True, act: str = "f16") -> np.ndarray:
     """``Linear._prep_activation`` (``_ops.py:337-365``) plus the INT8 smooth
     divide that only applies when there are no SmoothRot factors
-    (``_ops.py:529-533``)."""
-    x = np.asarray(x16, dtype=np.float16).reshape(-1, np.shape(x16)[-1])
+    (``_ops.py:529-533``).  ``act`` = "f16" (input and result float16) or
+    "bf16" (input and result float32 arrays holding bf16 values)."""
+    adt = np.float16 if act == "f16" else np.float32
+    x = np.asarray(x16, dtype=adt).reshape(-1, np.shape(x16)[-1])
     if smoothrot is not None:
-        x = div_f16(x, smoothrot)
+        x = div_f16(x, smoothrot, act)
     if rot_need:
-        x = rotate(x, rot_size)
+        x = rotate(x, rot_size, act)
     if w_in is not None and x.shape[1] < w_in:
-        x = np.concatenate([x, np.zeros((x.shape[0], w_in - x.shape[1]), np.float16)], 1)
+        x = np.concatenate([x, np.zeros((x.shape[0], w_in - x.shape[1]), adt)], 1)
     if perm is not None:
         x = x[:, np.asarray(perm, dtype=np.int64)]
     if int8_path and smoothrot is None and smooth is not None:
-        x = div_f16(x, smooth)
+        x = div_f16(x, smooth, act)
     return x
 
 

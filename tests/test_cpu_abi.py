@@ -50,6 +50,40 @@ def test_argument_validation_without_gpu(call, code):
     assert lib.ic_last_error().decode()
 
 
+def _gemm_a8_args(K, G, group_size, w_kind=None):
+    f = ctypes.c_void_p(256)   # aligned stand-in pointers: validation fails before any use
+    return [f, 64, K, K, f, L.IC_W_INT4 if w_kind is None else w_kind, 128, K // 2, f, G, group_size, f, None, 0,
+            None, None, f, L.IC_DTYPE_F16, 128, None]
+
+
+@pytest.mark.parametrize("K,G,gs", [(1024, 2, 512), (2048, 2, 1024)])
+def test_int4_group_scales_wider_than_256_rejected(K, G, gs):
+    """A 512-wide INT4 group's int32 partial can exceed the exact range of
+    the kernel's int -> float hand-off, so group_size > 256 is refused."""
+    lib = L.lib()
+    assert lib.ic_gemm_a8(*_gemm_a8_args(K, G, gs)) == L.IC_ERR_UNSUPPORTED
+    assert b"group_size 128 or 256" in lib.ic_last_error()
+
+
+def test_partial_last_group_rejected():
+    """K = 640 with 256-wide groups leaves a half group at the end (G = 3):
+    the kernel's accumulation units must be whole groups, so it is refused."""
+    lib = L.lib()
+    assert lib.ic_gemm_a8(*_gemm_a8_args(640, 3, 256)) == L.IC_ERR_UNSUPPORTED
+    assert b"multiple of group_size / 128" in lib.ic_last_error()
+
+
+def test_workspace_size_check_does_not_overflow():
+    """splits * M * N = 16 * 2^30 * 2^30 wraps int64 to 0; it is still refused."""
+    lib = L.lib()
+    f = ctypes.c_void_p(256)
+    M = N = 1 << 30
+    st = lib.ic_gemm_a8_splitk(f, M, 2048, 2048, f, L.IC_W_INT8, N, 2048, f, 1, 2048, f, None, 0, None, None, f,
+                               L.IC_DTYPE_F16, N, 16, f, 16, None)
+    assert st in (L.IC_ERR_ARG, L.IC_ERR_UNSUPPORTED)
+    assert lib.ic_last_error()
+
+
 def test_zero_sized_calls_are_no_ops():
     lib = L.lib()
     assert lib.ic_prep_quant(None, 0, 0, 64, 64, None, 0, 64, None, None, None, 0, None, None, None, None) == L.IC_OK

@@ -123,11 +123,11 @@ def test_int4_w4a8_group_scales_vs_oracle(dtype):
     x = h("int4_x").to(dtype)
     y = lin(x.cuda())
     assert y.dtype == dtype
-    x16 = x.float().numpy().astype(np.float16) if dtype == torch.float16 else None
-    if x16 is None:   # bf16 activations: oracle on the bf16 values via fp32
-        return
-    xp = O.prep_activation(x16, smoothrot=sd["weight_smoothrot_factors"].float().numpy(), rot_need=True,
-                           rot_size=256, w_in=512, perm=G["int4_perm"], int8_path=False)
+    # bf16 activations: the oracle runs on the bf16 values (float32 arrays)
+    act = "f16" if dtype == torch.float16 else "bf16"
+    x_in = x.float().numpy().astype(np.float16 if act == "f16" else np.float32)
+    xp = O.prep_activation(x_in, smoothrot=sd["weight_smoothrot_factors"].float().numpy(), rot_need=True,
+                           rot_size=256, w_in=512, perm=G["int4_perm"], int8_path=False, act=act)
     q, s = O.quantize_rows(xp)
     ref = O.gemm_a8(q, s, O.unpack_int4(G["int4_packed"], 512), sd["weight_scale"].float().numpy(),
                     bias=sd["bias"].numpy(), group_size=128)

@@ -79,6 +79,30 @@ def test_noalloc_splitk_matches_workspace_entry_two_calls():
         assert torch.isfinite(out_a.float()).all()
 
 
+@pytest.mark.gpu
+def test_noalloc_splitk_at_the_scratch_limit():
+    """A call whose partials fill the built-in scratch exactly (4 * 64 * 8192 =
+    2,097,152 floats) matches the workspace entry point; 65 tokens, one token
+    past the limit, are refused."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    c = _case(64, 8192, 1024, 8, True, 5, dev)
+    assert 4 * 64 * 8192 == SCRATCH_FLOATS
+    for _ in range(2):
+        st_a, out_a = _call(c, 4, noalloc=True, stream=stream)
+        st_b, out_b = _call(c, 4, noalloc=False, stream=stream)
+        torch.cuda.synchronize()
+        assert st_a == L.IC_OK and st_b == L.IC_OK, L.lib().ic_last_error()
+        assert O.max_rel(out_a.float().cpu().numpy(), out_b.float().cpu().numpy().astype(np.float64)) <= 1e-6
+    over = _case(65, 8192, 1024, 8, True, 6, dev)
+    st, _ = _call(over, 4, noalloc=True, stream=stream)
+    assert st == L.IC_ERR_ARG
+    assert b"exceeds the built-in scratch" in L.lib().ic_last_error()
+
+
 def test_noalloc_splitk_rejects_oversize_before_any_work():
     """splits * M * N above the built-in scratch is refused up front (no GPU
     work is queued, so this runs without a device too)."""
