@@ -38,6 +38,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = "comfyui-int-crush_b200"
 M, K, N, GS, ROT = 4096, 3072, 12288, 128, 256
 OPS = 2.0 * M * N * K
+# DRAM read + write bytes of one config-2 GEMM launch, from an ncu capture of
+# the GEMM kernel (bench.py --kernel-probe gemm)
+GEMM_TRAFFIC = 84.1e6
 
 
 def _pkg():
@@ -79,52 +82,88 @@ def make_inputs(seed: int = 0, device="cpu"):
 
 # ───────────────────────────── CPU baseline ─────────────────────────────────
 
-def cpu_baseline(sample_rows: int = 256, reps: int = 3, threads: int | None = None):
-    import torch
+CONFIG = {"workload": "config2_w4a8_linear M4096 K3072 N12288 g128 rot256 perm smoothrot bias",
+          "tokens_per_gpu": M, "l2": "flushed (256 MB write) between timed GPU steps"}
+
+
+def gpu_arm_config(world: int) -> dict:
+    """The ``config`` of the default line (both arms print the same)."""
+    return dict(CONFIG, parallelism=f"token-sharded dp{world} (no collective)",
+                weights="INT4 group-128, packed [12288, 1536] (GPU arm: repacked once at load)")
+
+
+def _cpu_layer(d, rows: int):
+    """One forward of the config-2 layer through the reference's PyTorch CPU
+    path (torch restatement, oracle/torch_reference_path.py): group-128
+    dequantisation of the weights (every call, as the reference does),
+    SmoothRot + rot 256 + perm prep, F.linear, plus the bias the GPU arm adds
+    (the reference's INT4 PyTorch path itself drops it)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import torch_reference_path as TR
-    if threads:
-        torch.set_num_threads(threads)
-    d = make_inputs()
-    xs = d["x"][:sample_rows]
-    times = []
+    y = TR.forward_int4_pytorch(d["x"][:rows], d["packed"], d["scale"], K, GS, smoothrot=d["smoothrot"],
+                                rot_size=ROT, w_in=K, perm=d["perm"])
+    return y.add_(d["bias"])
+
+
+def _time_cpu(d, rows: int, reps: int) -> float:
+    ts = []
     for i in range(reps + 1):
         t0 = time.perf_counter()
-        TR.forward_int4_pytorch(xs, d["packed"], d["scale"], K, GS, smoothrot=d["smoothrot"],
-                                rot_size=ROT, w_in=K, perm=d["perm"])
-        dt = time.perf_counter() - t0
+        _cpu_layer(d, rows)
         if i:
-            times.append(dt)
-    times.sort()
-    t = times[len(times) // 2]
-    tops = 2.0 * sample_rows * N * K / t / 1e12
-    return {"value": tops, "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{sample_rows} of {M} tokens of the config-2 layer, torch CPU fp16 "
-                      f"(dequant group-128 + F.linear + prep), median of {reps}, {t * 1e3:.1f} ms"}
+            ts.append(time.perf_counter() - t0)
+    ts.sort()
+    return ts[len(ts) // 2]
+
+
+def cpu_baseline(reps: int = 2) -> dict:
+    """The reference's CPU path on the whole 4096-token layer with every host
+    thread, plus a 256-token sample on one thread."""
+    import torch
+    d = make_inputs()
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    t = _time_cpu(d, M, reps)
+    torch.set_num_threads(1)
+    t1 = _time_cpu(d, 256, 1)
+    torch.set_num_threads(threads)
+    return {"value": OPS / t / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
+            "sample": f"all {M} tokens of the config-2 layer with bias, torch CPU fp16 (group-128 dequant + prep + "
+                      f"F.linear), median of {reps}: {t * 1e3:.0f} ms",
+            "one_thread": {"value": 2.0 * 256 * N * K / t1 / 1e12, "unit": "TOPS", "cores": 1,
+                           "sample": f"256 of {M} tokens, {t1 * 1e3:.0f} ms"}}
 
 
 def run_reference(args, rank: int) -> None:
+    """``--impl reference``: the reference's CPU path on the box's host cores,
+    each step the whole 4096-token config-2 layer (bias included), all host
+    threads.  Under torchrun only rank 0 runs and prints."""
     if rank != 0:
         return
     import torch
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
+    d = make_inputs()
     for _ in range(max(args.warmup, 1)):
-        cpu_baseline(64, reps=1)
+        _cpu_layer(d, M)
     steps = []
     for _ in range(args.steps):
-        r = cpu_baseline(256, reps=1)
-        steps.append(r["value"])
-    v = sorted(steps)[len(steps) // 2]
-    ms = 2.0 * M * N * K / (v * 1e12) * 1e3
+        t0 = time.perf_counter()
+        _cpu_layer(d, M)
+        steps.append(time.perf_counter() - t0)
+    ms = sum(steps) / len(steps) * 1e3
+    v = OPS / (ms * 1e-3) / 1e12
+    torch.set_num_threads(1)
+    t1 = _time_cpu(d, 256, 1)
     line = {"metric": "w4a8_linear_tops", "value": v, "unit": "TOPS", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "impl": "reference",
-            "config": {"workload": "config2_w4a8_linear M4096 K3072 N12288 g128 rot256 perm smoothrot",
-                       "sample_tokens": 256},
+            "impl": "reference", "config": gpu_arm_config(args.gpus),
+            "reference_run": "the reference's PyTorch CPU path on the host cores (rank 0 only)",
             "cpu_baseline": {"value": v, "unit": "TOPS", "cores": threads, "kind": "port",
-                             "sample": "256 of 4096 tokens per step, torch CPU path of the reference"},
+                             "sample": f"all {M} tokens per step, torch CPU path of the reference, bias included"},
+            "cpu_one_thread": {"value": 2.0 * 256 * N * K / t1 / 1e12, "unit": "TOPS", "cores": 1,
+                               "sample": f"256 of {M} tokens, {t1 * 1e3:.0f} ms"},
             "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -140,20 +179,23 @@ def _gpu_head_start(ms: float = 10.0) -> None:
 
 
 class Clocks:
-    """Samples nvidia-smi during the timed region."""
+    """Samples nvidia-smi clocks and throttle reasons during a timed region.
+    One sampler per node (local rank 0) covers all of the node's GPUs: a
+    sampler per rank stalled single steps by several ms."""
 
-    def __init__(self, idx: int):
-        self.idx = idx
+    def __init__(self, local_rank: int, n_gpus: int = 1):
+        self.active = local_rank == 0
+        self.n_gpus = n_gpus
         self.proc = None
         self.path = os.path.join("/tmp", f"ic_clocks_{os.getpid()}.csv")
 
     def __enter__(self):
-        if os.environ.get("INTCRUSH_NO_CLOCKS"):
+        if os.environ.get("INTCRUSH_NO_CLOCKS") or not self.active:
             return self
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.idx), "--query-gpu=clocks.sm,clocks.max.sm,power.draw,"
+                ["nvidia-smi", "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
                  "--format=csv,noheader,nounits", "-lms", os.environ.get("INTCRUSH_CLOCK_MS", "100")],
@@ -191,15 +233,47 @@ class Clocks:
     def summary(self):
         if os.environ.get("INTCRUSH_NO_CLOCKS"):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "sampling disabled"}
+        if not self.active:
+            return None
         try:
-            rows = [r.split(",") for r in open(self.path).read().strip().splitlines() if r.strip()]
-            sm = sorted(float(r[0]) for r in rows)
+            rows = [[c.strip() for c in r.split(",")] for r in open(self.path).read().strip().splitlines() if r.strip()]
+            rows = [r for r in rows if r[0].isdigit() and int(r[0]) < self.n_gpus]
+            sm = sorted(float(r[1]) for r in rows)
             names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-            reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].strip() == "Active"})
-            return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": float(rows[0][1]), "reasons": reasons,
-                    "samples": len(rows)}
+            reasons = sorted({names[i] for r in rows for i in range(4) if r[4 + i] == "Active"})
+            return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                    "samples": len(rows), "gpus_sampled": self.n_gpus}
         except Exception as e:  # pragma: no cover
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": str(e)}
+
+
+def _plugin_layer(rt, d, dev):
+    """The config-2 layer as the reference's plugin builds it: an
+    ``IntCrushOps.Linear`` (``make_intcrush_ops("int4_crush", 256)``) loaded
+    from the INT-Crush state-dict layout (packed INT4 weight, fp16 group
+    scales, perm, SmoothRot factors, bias).  ComfyUI itself is not installed
+    on the box; ``tests/comfy_stub.py`` provides the ``comfy.ops`` /
+    ``comfy.quant_ops`` classes the layer subclasses."""
+    import importlib
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import comfy_stub
+    comfy_stub.install()
+    importlib.import_module(PKG + ".quant_layout").register_intcrush_layouts()
+    ops = importlib.import_module(PKG + "._ops")
+    Ops = ops.make_intcrush_ops("int4_crush", ROT)
+    name = "double_blocks.0.img_mlp.0"
+    parent, lin = comfy_stub.make_parent(Ops.Linear, K, N, name=name)
+    parent.to(dev)
+    sd = {"weight": d["packed"].cpu(), "weight_scale": d["scale"].cpu(), "weight_perm": d["perm"].cpu(),
+          "weight_smoothrot_factors": d["smoothrot"].half().cpu(), "bias": d["bias"].cpu()}
+    parent.load_state_dict({f"{name}.{k}": v for k, v in sd.items()}, strict=False)
+    return lin
+
+
+def _step_stats(ms):
+    ms = sorted(ms)
+    return {"median": ms[len(ms) // 2], "max": ms[-1], "min": ms[0]}
 
 
 def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
@@ -229,7 +303,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with Clocks(local_rank) as clk:
+    with Clocks(local_rank, world) as clk:
         _gpu_head_start()   # after the sampler is up
         for i in range(2):   # untimed: the first steps after an idle GPU run slow
             flush.fill_(float(i))
@@ -249,15 +323,16 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         dist.barrier()
     prep_ms = [ev[i][0].elapsed_time(ev[i][1]) for i in range(args.steps)]
     gemm_ms = [ev[i][1].elapsed_time(ev[i][2]) for i in range(args.steps)]
-    if os.environ.get("INTCRUSH_BENCH_DEBUG"):
-        print(f"rank {rank} dev {torch.cuda.current_device()} gemm_ms {[round(v, 3) for v in gemm_ms]} "
-              f"prep_ms {[round(v, 3) for v in prep_ms]}", file=sys.stderr, flush=True)
+    # every rank's per-step times (stderr): an isolated slow step shows here
+    print(f"rank {rank} gemm_ms {[round(v, 3) for v in gemm_ms]} prep_ms {[round(v, 3) for v in prep_ms]}",
+          file=sys.stderr, flush=True)
     tot_ms = sum(prep_ms) + sum(gemm_ms)
 
-    # e2e: host-pinned input in, host-pinned output out, through the runtime
-    # API.  Three streams pipeline the steps: the input copy of step i+1 and
-    # the output copy of step i-1 overlap the compute of step i (two device
-    # buffers each way, ordered by events).
+    # e2e through the plugin call: IntCrushOps.Linear.forward, host-pinned
+    # input in, host-pinned output out.  Three streams pipeline the steps:
+    # the input copy of step i+1 and the output copy of step i-1 overlap the
+    # forward of step i (two device buffers each way, ordered by events).
+    lin = _plugin_layer(rt, d, dev)
     x_host = d["x"].cpu().pin_memory()
     out_host = [torch.empty((M, N), dtype=torch.float16).pin_memory() for _ in range(2)]
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
@@ -278,33 +353,38 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
             st.wait_event(ev_in[b])
             if i >= 2:
                 st.wait_event(ev_out[b])                # step i-2's output has left yd[b]
-            yd[b] = step(xd[b])
+            yd[b] = lin(xd[b])
             ev_cmp[b].record(st)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev_cmp[b])
                 out_host[b].copy_(yd[b], non_blocking=True)
                 ev_out[b].record(s_out)
 
-    e2e_steps(2)
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0.record(s_in)
-    s_in.wait_event(e0)
-    e2e_steps(args.steps)
-    s_out.wait_stream(st)
-    s_out.wait_stream(s_in)
-    e1.record(s_out)
-    torch.cuda.synchronize()
+    with torch.no_grad():
+        e2e_steps(2)
+        torch.cuda.synchronize()
+        # the plugin layer computes what the kernel step computes
+        plugin_equal = bool(torch.equal(lin(d["x"]), step(d["x"])))
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(s_in)
+        s_in.wait_event(e0)
+        e2e_steps(args.steps)
+        s_out.wait_stream(st)
+        s_out.wait_stream(s_in)
+        e1.record(s_out)
+        torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
 
     vals = torch.tensor([tot_ms, e2e_ms, sum(gemm_ms), sum(prep_ms)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     tot_ms, e2e_ms, gemm_sum, prep_sum = vals.tolist()
+    # DiT-block numbers at the same N (every rank takes part)
+    block = None if args.no_secondary else flux_block_secondary(args, rank, world, local_rank, dev, rt)
 
     if rank != 0:
         return
@@ -321,15 +401,14 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic",
-        "config": {"workload": "config2_w4a8_linear M4096 K3072 N12288 g128 rot256 perm smoothrot bias",
-                   "tokens_per_gpu": M, "parallelism": f"token-sharded dp{world} (no collective)",
-                   "l2": "flushed (256 MB write) between timed steps",
-                   "weights": "INT4 repacked once at load (ic_repack_int4 layout 0)"},
+        "config": gpu_arm_config(world),
         "e2e": {"value": world * OPS * args.steps / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS",
-                "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
+                "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
+                "path": "IntCrushOps.Linear.forward (the plugin layer), pinned host buffers",
+                "same_bits_as_kernel_step": plugin_equal},
         "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak, "unit": "TOPS",
-                     "frac": gemm_tops / int8_peak, "traffic": 84.1e6,
-                     "traffic_note": "bytes/launch, dram read+write from one ncu capture (profiles/gemm_tc_w4a8_grouped_config2.md)",
+                     "frac": gemm_tops / int8_peak, "traffic": GEMM_TRAFFIC,
+                     "traffic_note": "bytes/launch, dram read+write from one ncu capture of this GEMM",
                      "kernel": "gemm_tc_kernel<W_I4, grouped>",
                      "peak_source": f"2 x {src} bf16 cuBLAS ({bf16} TF/s), burst",
                      "kernel_ms": gemm_avg},
@@ -339,8 +418,11 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
         "wall_ms": t_wall * 1e3,
         "clocks": clk.summary(),
     }
+    if block is not None:
+        line.setdefault("secondary", {})["flux_block"] = block
     if world == 1 and not args.no_secondary:
-        line["secondary"] = secondary_lines(dev, flush, hbm, int8_peak, bf16)
+        line.setdefault("secondary", {}).update(secondary_lines(dev, flush, hbm, int8_peak, bf16))
+        line["secondary"]["gpu_comparators"] = gpu_comparators(dev, flush, d, w_rep, perm32)
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline()
     print(json.dumps(line), flush=True)
@@ -369,7 +451,7 @@ def run_features(args, rank: int, world: int, local_rank: int) -> None:
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with Clocks(local_rank) as clk:
+    with Clocks(local_rank, world) as clk:
         _gpu_head_start()   # after the sampler is up
         for i in range(2):   # untimed: the first steps after an idle GPU run slow
             flush.fill_(float(i))
@@ -474,6 +556,154 @@ def secondary_lines(dev, flush, hbm_gbs: float, int8_peak: float, bf16_peak: flo
             "tflops": fl / (ms * 1e-3) / 1e12, "bf16_frac": fl / (ms * 1e-3) / 1e12 / bf16_peak,
             "kernels": 2, "note": "low-rank down + W4A16 with the LoRA term fused"}
     return out
+
+
+def gpu_comparators(dev, flush, d, w_rep, perm32, reps: int = 10) -> dict:
+    """The library GPU paths the reference falls back to, timed on the same
+    box next to this library's kernels (CUDA events, L2 flushed before each
+    call, median of ``reps``).
+
+    * ``torch._int_mm`` (cuBLAS int8) + dequantisation in torch: the
+      reference's W8A8 / W4A8 math without its Triton kernels; for W4A8 also
+      with the per-call INT4 -> INT8 unpack the reference's W4A8 path does
+      (``_ops.py:448-457``), here in torch ops.
+    * torch dequantisation (INT4 -> fp16 with group scales) + ``F.linear``:
+      the reference's PyTorch INT4 path on the GPU (``_ops.py:483-491``).
+    The reference's Triton kernels themselves are not on the box: the
+    reference's Python sources do not travel with this repository."""
+    import torch
+    import torch.nn.functional as F
+    rt = _pkg()
+    st = torch.cuda.current_stream()
+
+    def timed(fn):
+        fn()
+        ts = []
+        for i in range(reps):
+            flush.fill_(float(i))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return sorted(ts)[len(ts) // 2]
+
+    def unpack_i8(p):
+        lo = ((p & 0xF).to(torch.int16) ^ 8) - 8
+        hi = ((p >> 4).to(torch.int16) ^ 8) - 8
+        return torch.stack([lo, hi], dim=-1).reshape(p.shape[0], -1).to(torch.int8)
+
+    out = {}
+    g = torch.Generator().manual_seed(5)
+    # W4A8 per channel at the config-2 shape
+    xq, s_a, _, _ = rt.prep_quantize(d["x"], smoothrot=d["smoothrot"], rot_size=ROT, w_in=K, perm=perm32)
+    xq = xq.contiguous()
+    s_n = d["scale"][:, 0].float().contiguous()
+    w8 = unpack_i8(d["packed"])
+    bias = d["bias"]
+
+    def torch_w4a8(unpack):
+        w = unpack_i8(d["packed"]) if unpack else w8
+        acc = torch._int_mm(xq, w.t())
+        return (acc.float() * s_a[:, None] * s_n[None, :] + bias.float()).half()
+    t_ours = timed(lambda: rt.gemm_a8(xq, w_rep, s_n, s_a, bias=bias, out_dtype=torch.float16, repacked=True))
+    t_mm = timed(lambda: torch_w4a8(False))
+    t_mm_u = timed(lambda: torch_w4a8(True))
+    out["w4a8_per_channel_4096x12288x3072"] = {
+        "ours_ms": t_ours, "int_mm_dequant_ms": t_mm, "unpack_int_mm_dequant_ms": t_mm_u,
+        "ratio_vs_int_mm": t_mm / t_ours, "ratio_vs_unpack_int_mm": t_mm_u / t_ours}
+    # W8A8 per channel: config-1 shape and the config-2 GEMM shape
+    for (mm, nn, kk) in ((256, 3072, 3072), (4096, 12288, 3072)):
+        xa = torch.randint(-128, 128, (mm, kk), generator=g, dtype=torch.int8).to(dev)
+        wb = torch.randint(-127, 128, (nn, kk), generator=g, dtype=torch.int8).to(dev)
+        sa = (torch.rand(mm, generator=g) * 5e-2 + 1e-3).to(dev)
+        sb = (torch.rand(nn, generator=g) * 1e-2 + 1e-3).to(dev)
+        bb = (torch.randn(nn, generator=g) * 0.02).half().to(dev)
+        t_ours = timed(lambda: rt.gemm_a8(xa, wb, sb, sa, bias=bb, out_dtype=torch.float16))
+        t_mm = timed(lambda: (torch._int_mm(xa, wb.t()).float() * sa[:, None] * sb[None, :] + bb.float()).half())
+        out[f"w8a8_{mm}x{nn}x{kk}"] = {"ours_ms": t_ours, "int_mm_dequant_ms": t_mm, "ratio": t_mm / t_ours}
+    # W4A16 (configs[2]): torch dequantisation + F.linear
+    N3 = K3 = 3072
+    q = torch.randint(-8, 8, (N3, K3), generator=g, dtype=torch.int8)
+    qu = (q.to(torch.int16) & 0xF).to(torch.uint8)
+    packed = (qu[:, 0::2] | (qu[:, 1::2] << 4)).contiguous().to(dev)
+    w1 = rt.repack_int4(packed, K3, 1)
+    sc = (torch.rand(N3, K3 // 128, generator=g) * (2e-2 - 1e-3) + 1e-3).half().to(dev)
+
+    def dequant_f16():
+        wq = unpack_i8(packed).float().reshape(N3, -1, 128) * sc.float().unsqueeze(2)
+        return wq.reshape(N3, K3).half()
+    for M3 in (1, 16, 256):
+        x3 = torch.randn(M3, K3, generator=g).half().to(dev)
+        t_ours = timed(lambda: rt.gemm_w4a16(x3, w1, sc, group_size=128, w_layout=1))
+        t_t = timed(lambda: F.linear(x3, dequant_f16()))
+        out[f"w4a16_m{M3}"] = {"ours_ms": t_ours, "torch_dequant_linear_ms": t_t, "ratio": t_t / t_ours}
+    return out
+
+
+def flux_block_secondary(args, rank: int, world: int, local_rank: int, dev, rt, steps: int = 5) -> dict:
+    """The Flux-class double block at this run's N: every rank
+    runs one sample (token sharding, no collective); at N > 1 also one sample
+    split over the ranks (sequence parallel, K/V all-gather over NCCL) and the
+    time of the block's K/V all-gathers alone.  tokens/s over all ranks,
+    block time = max over ranks."""
+    import torch
+    import torch.distributed as dist
+    blk = FluxDoubleBlock(rt, dev)
+    g = torch.Generator().manual_seed(100 + rank)
+    img = torch.randn(1, 4096, 3072, generator=g).half().to(dev)
+    txt = torch.randn(1, 512, 3072, generator=g).half().to(dev)
+    vec = torch.randn(1, 3072, generator=g).half().to(dev)
+    st = torch.cuda.current_stream()
+
+    def timed_block(im):
+        with torch.no_grad():
+            for _ in range(2):
+                blk(im, txt, vec)
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(steps):
+                blk(im, txt, vec)
+            e1.record(st)
+            torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    n_tok = 4096 + 512
+    ms = timed_block(img)
+    res = {"tokens_per_s": world * n_tok / (ms * 1e-3), "block_ms": ms, "n_gpus": world,
+           "layout": f"token-sharded x{world} (one sample per GPU, no collective)",
+           "linear_tops": world * blk.linear_ops(4096, 512) / (ms * 1e-3) / 1e12}
+    if world > 1:
+        blk.sp_group = dist.group.WORLD
+        per = 4096 // world
+        mine = img[:, rank * per:(rank + 1) * per].contiguous()
+        ms_sp = timed_block(mine)
+        kv = torch.randn(2, 1, 24, per, 128, generator=g).half().to(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(2):
+            _gather_tokens(kv[0], dist.group.WORLD)
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(steps):
+            _gather_tokens(kv[0], dist.group.WORLD)
+            _gather_tokens(kv[1], dist.group.WORLD)
+        e1.record(st)
+        torch.cuda.synchronize()
+        ag = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(ag, op=dist.ReduceOp.MAX)
+        res["sequence_parallel"] = {
+            "tokens_per_s": n_tok / (ms_sp * 1e-3), "block_ms": ms_sp,
+            "kv_all_gather_ms": ag.item(),
+            "layout": f"one sample over {world} GPUs: image tokens split, text replicated, K/V all-gather (NCCL)"}
+        blk.sp_group = None
+    return res
 
 
 class _QLinear:
@@ -701,7 +931,7 @@ def run_wan(args, rank: int, world: int, local_rank: int) -> None:
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-        with Clocks(local_rank) as clk:
+        with Clocks(local_rank, world) as clk:
             _gpu_head_start()
             for i in range(args.steps):
                 ev[i][0].record(st)
@@ -764,7 +994,7 @@ def run_block(args, rank: int, world: int, local_rank: int) -> None:
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-        with Clocks(local_rank) as clk:
+        with Clocks(local_rank, world) as clk:
             _gpu_head_start()   # after the sampler is up
             for i in range(2):   # untimed: the first steps after an idle GPU run slow
                 flush.fill_(float(i))

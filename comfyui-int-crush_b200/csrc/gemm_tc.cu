@@ -96,9 +96,13 @@ constexpr float kMagicF = 12582912.0f; // 1.5 * 2^23
 // weight tiles (P, by TMA, deep), the expanded weight tiles (W, written by the
 // expansion warps) and the activation tiles (X, by TMA) -- so that the TMA
 // latency of the packed stream is hidden independently of the MMA ring.
-template <int MODE, int BN, bool GROUPED>
+template <int MODE, int BN, bool GROUPED, bool PAIR = false>
 struct Cfg {
   static constexpr bool I4 = (MODE != W_I8);
+  // CTA pairs: the pair's tile is 256 weight rows x BN tokens; each CTA
+  // holds 128 of the weight rows and BN / 2 of the token rows
+  static constexpr int XROWS = PAIR ? BN / 2 : BN;
+  static constexpr int TILE_N = PAIR ? 2 * kTileN : kTileN;
   // epilogue warps: group-scaled tiles keep 64 fp32 accumulators per thread
   // (one warp per 32 TMEM lanes x 64 columns); per-channel tiles stream.
   // (BN = 160, group-scaled: 8 warps of 80 columns, so that three accumulator
@@ -107,7 +111,7 @@ struct Cfg {
   static constexpr int CPT = BN / (EPI / 4);                      // columns per epilogue thread
   static constexpr int THREADS = 32 * (4 + EPI);
   static constexpr int W_BYTES = kTileN * 128;                    // 16 KB
-  static constexpr int X_BYTES = BN * 128;
+  static constexpr int X_BYTES = XROWS * 128;
   static constexpr int P_BYTES = (MODE == W_I4) ? kTileN * 64 : (MODE == W_I4F ? kTileN * 32 : 0);
   // group-scaled tiles: four accumulator buffers when they fit in TMEM, and
   // two 1 KB constant atoms (the operands of the re-arming MMA) at offset 0
@@ -134,6 +138,7 @@ struct Cfg {
   static_assert(S_X >= 2, "pipeline depth");
   static_assert(!(GROUPED && MODE == W_I4F), "W4A16 folds scales into the weights");
   static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(!PAIR || (MODE != W_I4F && BN % 32 == 0), "pair tiles: A8 kinds, BN / 2 a multiple of 16");
   static_assert(TMEM_COLS_RAW <= 512, "tensor memory");
 };
 
@@ -294,11 +299,11 @@ __device__ unsigned long long g_ic_trace[16];
 #define IC_TADD(i)
 #endif
 
-template <int MODE, int BN, bool GROUPED>
-__global__ void __launch_bounds__(Cfg<MODE, BN, GROUPED>::THREADS, 1)
+template <int MODE, int BN, bool GROUPED, bool PAIR>
+__global__ void __launch_bounds__(Cfg<MODE, BN, GROUPED, PAIR>::THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                const GemmArgs a) {
-  using C = Cfg<MODE, BN, GROUPED>;
+  using C = Cfg<MODE, BN, GROUPED, PAIR>;
   constexpr int SX = C::S_X, SW = C::S_W, SP = C::S_P;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -312,11 +317,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   uint64_t* acc_full = p_full + SP;           // [NB] MMA commit -> epilogue
   uint64_t* acc_empty = acc_full + NB;        // [NB] epilogue -> MMA (count EPI)
   uint64_t* drain = acc_empty + NB;           // abort path: MMA completion
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 2);
+  uint64_t* fin = drain + 1;                  // pairs: end-of-kernel handshake
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 3);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // CTA pairs: rank 0 (the leader) issues the pair MMAs and owns the
+  // barriers they wait on (operands full, accumulator free); both CTAs own
+  // the barriers the MMA commits release (operands free, accumulator full)
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = (rank == 0);
+  auto lead = [&](uint64_t* bar) -> uint32_t { return mapa_u32(smem_u32(bar), 0u); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < SX; ++s) {
@@ -324,21 +336,27 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       mbar_init(&x_empty[s], 1);
     }
     for (int s = 0; s < SW; ++s) {
-      mbar_init(&w_full[s], 1);
+      mbar_init(&w_full[s], PAIR ? 2 : 1);
       mbar_init(&w_empty[s], 1);
     }
     for (int s = 0; s < SP; ++s) mbar_init(&p_full[s], 1);
     for (int b = 0; b < NB; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], C::EPI);
+      mbar_init(&acc_empty[b], PAIR ? 2 * C::EPI : C::EPI);
     }
     mbar_init(drain, 1);
+    mbar_init(fin, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc2(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish2();
+    } else {
+      tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tm_w);
@@ -354,10 +372,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();   // the peer's barriers are initialised
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   const int total_units = a.m_tiles * a.n_tiles * a.splits;
+  const int wu0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int wu_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int row0 = (int)rank * kTileN;   // this CTA's first weight row inside the tile
   // accumulation units (one K group each when GROUPED) per work unit
   const int units = GROUPED ? a.kb_per_unit / a.kb_per_group : 1;
 
@@ -372,7 +394,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int wu = blockIdx.x; ok && wu < total_units; wu += gridDim.x) {
+      for (int wu = wu0; ok && wu < total_units; wu += wu_step) {
         const int tile = wu / a.splits, kb_lo = (wu % a.splits) * a.kb_per_unit;
         int n_blk, m_blk;
         tile_nm(a, tile, n_blk, m_blk);
@@ -380,14 +402,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           const int s = it % SX;
           const uint32_t ph = (uint32_t)(it / SX) & 1u;
           { IC_T0();
-          if (!mbar_wait(&x_empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
+          const bool got = PAIR ? mbar_wait_cl(&x_empty[s], ph ^ 1u, abort_flag)
+                                : mbar_wait(&x_empty[s], ph ^ 1u, abort_flag);
+          if (!got) { ok = false; break; }
           IC_TADD(8); }
-          mbar_arrive_expect_tx(&x_full[s], (uint32_t)C::XSTAGE);
-          tma_load_2d(x_stage(s), &tm_x, &x_full[s], kb * C::KB_ELEMS, m_blk * BN);
-          if constexpr (MODE == W_I8) tma_load_2d(w_stage(s), &tm_w, &x_full[s], kb * 128, n_blk * kTileN);
+          if constexpr (PAIR) {
+            // both halves land on the leader's barrier; the leader expects them
+            if (leader) mbar_arrive_expect_tx(&x_full[s], (uint32_t)(2 * C::XSTAGE));
+            tma_load_2d_pair(x_stage(s), &tm_x, lead(&x_full[s]), kb * C::KB_ELEMS, m_blk * BN + (int)rank * C::XROWS);
+            if constexpr (MODE == W_I8)
+              tma_load_2d_pair(w_stage(s), &tm_w, lead(&x_full[s]), kb * 128, n_blk * C::TILE_N + row0);
+          } else {
+            mbar_arrive_expect_tx(&x_full[s], (uint32_t)C::XSTAGE);
+            tma_load_2d(x_stage(s), &tm_x, &x_full[s], kb * C::KB_ELEMS, m_blk * BN);
+            if constexpr (MODE == W_I8) tma_load_2d(w_stage(s), &tm_w, &x_full[s], kb * 128, n_blk * kTileN);
+          }
         }
       }
-      if (!ok) {
+      // (the peer's loads complete on the leader's barriers: only the leader
+      // can wait for them; it does so below)
+      if (!ok && (!PAIR || leader)) {
         volatile int never = 0;
         const int first = it > SX ? it - SX : 0;
         for (int j = first; j < it; ++j) mbar_wait(&x_full[j % SX], (uint32_t)(j / SX) & 1u, &never);
@@ -395,38 +429,47 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = (MODE == W_I4F) ? idesc_f16(kTileN, BN, false) : idesc_i8(kTileN, BN);
+    if (lane == 0 && (!PAIR || leader)) {
+      constexpr int MM = PAIR ? 2 * kTileN : kTileN;
+      const uint32_t idesc = (MODE == W_I4F) ? idesc_f16(MM, BN, false) : idesc_i8(MM, BN);
       // GROUPED: the re-arming MMA (kind::f16, K = 16, accumulate off) writes
       // 1.5 * 2^23 as fp32 into every element of the buffer; the group's
       // kind::i8 MMAs then add the int32 partial onto those bits.  SBO = 0 makes
       // all 8-row groups of an operand read the same 1 KB atom.
-      const uint32_t idesc_m = idesc_f16(kTileN, BN, false);
+      const uint32_t idesc_m = idesc_f16(MM, BN, false);
       const uint64_t magic_a = smem_desc_sw128(smem_u32(smem)) & ~(0x3FFFull << 32);
       const uint64_t magic_b = smem_desc_sw128(smem_u32(smem + 1024)) & ~(0x3FFFull << 32);
       int it = 0, uc = 0;
       bool ok = true;
-      for (int wu = blockIdx.x; ok && wu < total_units; wu += gridDim.x) {
+      // the peer's operands and free accumulators are counted on these
+      // barriers too: cluster-scope acquires for the pair form
+      auto wait_any = [&](uint64_t* bar, uint32_t par) {
+        return PAIR ? mbar_wait_cl(bar, par, abort_flag) : mbar_wait(bar, par, abort_flag);
+      };
+      for (int wu = wu0; ok && wu < total_units; wu += wu_step) {
         const int kb_lo = (wu % a.splits) * a.kb_per_unit;
         for (int u = 0; ok && u < units; ++u, ++uc) {
           const int kb0 = GROUPED ? kb_lo + u * a.kb_per_group : kb_lo;
           const int kb1 = GROUPED ? min(kb0 + a.kb_per_group, kb_lo + a.kb_per_unit) : kb_lo + a.kb_per_unit;
           const int b = uc % NB;
           { IC_T0();
-          if (!mbar_wait(&acc_empty[b], (uint32_t)(uc / NB) & 1u, abort_flag)) { ok = false; break; }
+          if (!wait_any(&acc_empty[b], (uint32_t)(uc / NB) & 1u)) { ok = false; break; }
           IC_TADD(0); }
           tc_fence_after();
           const uint32_t d = tmem_base + (uint32_t)(b * BN);
-          if constexpr (GROUPED) mma_f16(d, magic_a, magic_b, idesc_m, 0u);
+          if constexpr (GROUPED) {
+            if constexpr (PAIR) mma_f16_2(d, magic_a, magic_b, idesc_m, 0u);
+            else mma_f16(d, magic_a, magic_b, idesc_m, 0u);
+          }
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const int sx = it % SX;
             { IC_T0();
-            if (!mbar_wait(&x_full[sx], (uint32_t)(it / SX) & 1u, abort_flag)) { ok = false; break; }
+            if (!wait_any(&x_full[sx], (uint32_t)(it / SX) & 1u)) { ok = false; break; }
             IC_TADD(1); }
             const int sw = C::I4 ? it % SW : sx;
             if constexpr (C::I4) {
               IC_T0();
-              if (!mbar_wait(&w_full[sw], (uint32_t)(it / SW) & 1u, abort_flag)) { ok = false; break; }
+              if (!wait_any(&w_full[sw], (uint32_t)(it / SW) & 1u)) { ok = false; break; }
               IC_TADD(2);
             }
             tc_fence_after();
@@ -436,18 +479,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
             for (int k = 0; k < 4; ++k) {
               const uint32_t acc = GROUPED ? 1u : ((kb > kb0 || k > 0) ? 1u : 0u);
               if constexpr (MODE == W_I4F) mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, acc);
+              else if constexpr (PAIR) mma_i8_2(d, adesc + 2 * k, bdesc + 2 * k, idesc, acc);
               else mma_i8(d, adesc + 2 * k, bdesc + 2 * k, idesc, acc);
             }
-            mma_commit(&x_empty[sx]);
-            if constexpr (C::I4) mma_commit(&w_empty[sw]);
+            if constexpr (PAIR) {
+              mma_commit2_both(&x_empty[sx]);
+              if constexpr (C::I4) mma_commit2_both(&w_empty[sw]);
+            } else {
+              mma_commit(&x_empty[sx]);
+              if constexpr (C::I4) mma_commit(&w_empty[sw]);
+            }
           }
           if (!ok) break;
-          mma_commit(&acc_full[b]);
+          if constexpr (PAIR) mma_commit2_both(&acc_full[b]);
+          else mma_commit(&acc_full[b]);
         }
       }
       if (!ok) {
         volatile int never = 0;
-        mma_commit(drain);
+        if constexpr (PAIR) mma_commit2_local(drain);
+        else mma_commit(drain);
         mbar_wait(drain, 0, &never);
       }
     }
@@ -460,14 +511,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       const int xw = warp - 2;
       int issued = 0;
       auto issue_p = [&](int j) {
-        const int wu_j = blockIdx.x + (j / a.kb_per_unit) * gridDim.x;
+        const int wu_j = wu0 + (j / a.kb_per_unit) * wu_step;
         if (wu_j >= total_units) return;
         const int kb = (wu_j % a.splits) * a.kb_per_unit + j % a.kb_per_unit;
         int n_blk, m_unused;
         tile_nm(a, wu_j / a.splits, n_blk, m_unused);
         const int sp = j % SP;
         mbar_arrive_expect_tx(&p_full[sp], (uint32_t)C::P_BYTES);
-        tma_load_2d(p_stage(sp), &tm_w, &p_full[sp], kb * (MODE == W_I4 ? 64 : 32), n_blk * kTileN);
+        tma_load_2d(p_stage(sp), &tm_w, &p_full[sp], kb * (MODE == W_I4 ? 64 : 32), n_blk * C::TILE_N + row0);
         issued = j + 1;
       };
       if (lane == 0)
@@ -475,7 +526,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       int it = 0;
       bool ok = true;
       const bool rp = a.w_repacked != 0;
-      for (int wu = blockIdx.x; ok && wu < total_units; wu += gridDim.x) {
+      for (int wu = wu0; ok && wu < total_units; wu += wu_step) {
         int n_blk, m_unused;
         tile_nm(a, wu / a.splits, n_blk, m_unused);
         const int kb_lo = (wu % a.splits) * a.kb_per_unit;
@@ -488,7 +539,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
 #if defined(IC_TRACE)
           _t0 = clock64();
 #endif
-          if (w_ok) w_ok = mbar_wait(&w_empty[sw], ((uint32_t)(it / SW) & 1u) ^ 1u, abort_flag);
+          if (w_ok)
+            w_ok = PAIR ? mbar_wait_cl(&w_empty[sw], ((uint32_t)(it / SW) & 1u) ^ 1u, abort_flag)
+                        : mbar_wait(&w_empty[sw], ((uint32_t)(it / SW) & 1u) ^ 1u, abort_flag);
           if (lane == 0) IC_TADD(6);
 #if defined(IC_TRACE)
           _t0 = clock64();
@@ -585,7 +638,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           __syncwarp();
           if (lane == 0) IC_TADD(9);
           if (lane == 0) {
-            mbar_arrive(&w_full[sw]);
+            if constexpr (PAIR) mbar_arrive_cluster(lead(&w_full[sw]));   // the leader's MMA reads it
+            else mbar_arrive(&w_full[sw]);
             issue_p(it + SP);   // same parity as it: this warp's next use of the stage
           }
         }
@@ -605,15 +659,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     constexpr float wmul = (MODE == W_I4) ? 0.0625f : 1.0f;   // int4 held as 16*q
     tc_fence_before();
     __syncwarp();
+    // the accumulator buffers are free: counted on the leader for pairs
+    auto acc_free = [&](int b) {
+      if constexpr (PAIR) mbar_arrive_cluster(lead(&acc_empty[b]));
+      else mbar_arrive(&acc_empty[b]);
+    };
+    auto acc_wait = [&](int b, uint32_t par) {
+      return PAIR ? mbar_wait_cl(&acc_full[b], par, abort_flag) : mbar_wait(&acc_full[b], par, abort_flag);
+    };
     if (lane == 0)
-      for (int b = 0; b < NB; ++b) mbar_arrive(&acc_empty[b]);
+      for (int b = 0; b < NB; ++b) acc_free(b);
     int uc = 0;
     bool ok = true;
-    for (int wu = blockIdx.x; ok && wu < total_units; wu += gridDim.x) {
+    for (int wu = wu0; ok && wu < total_units; wu += wu_step) {
       const int tile = wu / a.splits, split = wu % a.splits;
       int n_blk, m_blk;
       tile_nm(a, tile, n_blk, m_blk);
-      const int n = n_blk * kTileN + 32 * q + lane;
+      const int n = n_blk * C::TILE_N + row0 + 32 * q + lane;
       const bool nvalid = n < a.N;
       const float bias_n = (nvalid && a.bias) ? load_any(a.bias, a.bias_dtype, n) : 0.f;
       const float zpc_n = (nvalid && a.zp_corr) ? a.zp_corr[n] : 0.f;
@@ -630,7 +692,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           // next group's scale is fetched while this group is consumed
           const float sw_next = (nvalid && u + 1 < units) ? __ldg(swrow + u + 1) * wmul : 0.f;
           IC_T0();
-          if (!mbar_wait(&acc_full[b], (uint32_t)(uc / NB) & 1u, abort_flag)) { ok = false; break; }
+          if (!acc_wait(b, (uint32_t)(uc / NB) & 1u)) { ok = false; break; }
           if (warp == 4 && lane == 0) IC_TADD(3);
 #if defined(IC_TRACE)
           _t0 = clock64();
@@ -649,7 +711,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[b]);
+          if (lane == 0) acc_free(b);
           const unsigned long long sw2 = pack2(sw, sw);
 #pragma unroll
           for (int c = 0; c < C32; ++c)
@@ -679,7 +741,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       } else {
         const int b = uc % NB;
         const float sw = (MODE == W_I4F) ? 1.f : (nvalid ? __ldg(&a.s_w[n]) * wmul : 0.f);
-        if (!mbar_wait(&acc_full[b], (uint32_t)(uc / NB) & 1u, abort_flag)) { ok = false; break; }
+        if (!acc_wait(b, (uint32_t)(uc / NB) & 1u)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < C::CPT / 32; ++c) {
@@ -697,7 +759,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[b]);
+        if (lane == 0) acc_free(b);
         ++uc;
       }
     }
@@ -707,9 +769,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
   if (threadIdx.x == 0) { IC_T0(); (void)_t0; }
 #endif
   __syncthreads();
+  if constexpr (PAIR) {
+    // Neither CTA may leave while the other can still reach its shared
+    // memory (remote arrivals, TMA bytes counted on the leader, the leader's
+    // MMAs reading the peer's operands): each tells the other it is done and
+    // waits (bounded) for the same word back.
+    if (threadIdx.x == 0) {
+      volatile int never = 0;
+      mbar_arrive_cluster(mapa_u32(smem_u32(fin), rank ^ 1u));
+      mbar_wait_cl(fin, 0, &never);
+    }
+    __syncthreads();
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc2(tmem_base, C::TMEM_COLS);
+    else tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -760,17 +835,49 @@ int num_sms() {
   return n;
 }
 
-template <int MODE, int BN, bool GROUPED>
+template <int MODE, int BN, bool GROUPED, bool PAIR = false>
 static cudaError_t launch_gemm_t(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a,
                                  cudaStream_t st) {
-  using C = Cfg<MODE, BN, GROUPED>;
-  auto kern = gemm_tc_kernel<MODE, BN, GROUPED>;
+  using C = Cfg<MODE, BN, GROUPED, PAIR>;
+  auto kern = gemm_tc_kernel<MODE, BN, GROUPED, PAIR>;
   cudaError_t e = set_smem_once(kern, C::SMEM);
   if (e != cudaSuccess) return e;
   const int tiles = a.m_tiles * a.n_tiles * a.splits;   // work units
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, C::THREADS, C::SMEM, st>>>(tw, tx, a);
-  return cudaGetLastError();
+  if constexpr (!PAIR) {
+    const int grid = tiles < num_sms() ? tiles : num_sms();
+    kern<<<grid, C::THREADS, C::SMEM, st>>>(tw, tx, a);
+    return cudaGetLastError();
+  } else {
+    // one CTA pair (cluster of 2) per pair of SMs, persistent over the tiles
+    const int pairs = num_sms() / 2;
+    const int grid = 2 * (tiles < pairs ? tiles : pairs);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((unsigned)C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, tw, tx, a);
+  }
+}
+
+// CTA pairs (tcgen05 cta_group::2) for large problems: the pair shares one
+// 256-row x BN-token tile, each CTA stages half of the token rows, which
+// halves the activation traffic through each SM's shared memory per MAC.
+// INTCRUSH_PAIR=0 keeps one CTA per tile (A/B comparisons).
+static bool pair_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("INTCRUSH_PAIR");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
 }
 
 // Token-tile width for M tokens.  INTCRUSH_FORCE_BN (32/64/128/192/256)
@@ -821,11 +928,62 @@ static cudaError_t dispatch_bn(int bn, const CUtensorMap& tw, const CUtensorMap&
 }
 
 // Entry used by ic_gemm_a8: xq [M, ldq] int8, w int8/int4.
+// Pair tile width for M x N, or 0 when pairs do not apply: one CTA pair per
+// tile, enough tiles to give every pair of SMs several.
+static int pick_pair_bn(int M, int N, bool grouped, int splits) {
+  if (!pair_enabled() || splits != 1 || forced_bn()) return 0;
+  static const int env_bn = [] { const char* e = getenv("INTCRUSH_PAIR_BN"); return e ? atoi(e) : 0; }();   // tuning
+  const int bn = (grouped && (env_bn == 128 || env_bn == 160 || env_bn == 192)) ? env_bn : (grouped ? 192 : 256);
+  const long long tiles = (long long)((M + bn - 1) / bn) * ((N + 2 * kTileN - 1) / (2 * kTileN));
+  return tiles >= (long long)num_sms() ? bn : 0;   // >= 2 tiles per pair
+}
+
+template <int MODE>
+static cudaError_t launch_pair(int bn, const CUtensorMap& tw, const CUtensorMap& tx, GemmArgs a, cudaStream_t st) {
+  a.m_tiles = (a.M + bn - 1) / bn;
+  a.n_tiles = (a.N + 2 * kTileN - 1) / (2 * kTileN);
+  a.group_m = 16 < a.m_tiles ? 16 : a.m_tiles;
+  if (a.G > 1) {
+    switch (bn) {
+      case 128: return launch_gemm_t<MODE, 128, true, true>(tw, tx, a, st);
+      case 160: return launch_gemm_t<MODE, 160, true, true>(tw, tx, a, st);
+      case 192: return launch_gemm_t<MODE, 192, true, true>(tw, tx, a, st);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  if (bn != 256) return cudaErrorInvalidValue;
+  return launch_gemm_t<MODE, 256, false, true>(tw, tx, a, st);
+}
+
 cudaError_t launch_gemm_a8(const int8_t* xq, int M, int K, long long ldq, const void* w, int w_kind,
                            int N, long long ldw, GemmArgs a, int force_bn, cudaStream_t st,
                            const char** why) {
   CUtensorMap tx, tw;
   const bool grouped = a.G > 1;
+  const int pbn = force_bn ? 0 : pick_pair_bn(M, N, grouped, a.splits < 1 ? 1 : a.splits);
+  if (pbn) {
+    if (!make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, (uint64_t)K, (uint64_t)M, (uint64_t)ldq, 128,
+                   (uint32_t)(pbn / 2), CU_TENSOR_MAP_SWIZZLE_128B)) {
+      *why = "cuTensorMapEncodeTiled failed for the activation operand";
+      return cudaErrorInvalidValue;
+    }
+    bool okw;
+    if (w_kind == IC_W_INT8)
+      okw = make_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, 128,
+                      kTileN, CU_TENSOR_MAP_SWIZZLE_128B);
+    else
+      okw = make_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)((K + 1) / 2), (uint64_t)N,
+                      (uint64_t)ldw, 64, kTileN, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!okw) {
+      *why = "cuTensorMapEncodeTiled failed for the weight operand";
+      return cudaErrorInvalidValue;
+    }
+    a.M = M; a.N = N; a.K = K;
+    a.num_kb = (K + 127) / 128;
+    a.splits = 1;
+    a.kb_per_unit = a.num_kb;
+    return w_kind == IC_W_INT8 ? launch_pair<W_I8>(pbn, tw, tx, a, st) : launch_pair<W_I4>(pbn, tw, tx, a, st);
+  }
   const int bn = force_bn ? force_bn : pick_bn(M, N, grouped);
   if (!make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, (uint64_t)K, (uint64_t)M, (uint64_t)ldq, 128,
                  (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B)) {

@@ -23,36 +23,12 @@
 // A thread applies up to 4 index bits (16 values) of butterflies in registers
 // per pass; passes exchange through a padded fp64 shared buffer.
 #include "ic_common.cuh"
+#include "prep_common.cuh"
 
 
 namespace ic {
 
-struct PrepArgs {
-  const void* x;
-  int64_t M, K, ldx;
-  const float* smoothrot;
-  int64_t w_in;
-  const int32_t* perm;
-  const float* smooth;
-  int8_t* xq;
-  int64_t ldq;
-  float* s_a;
-  void* x_prep;
-  float* rowsum;
-  int64_t Kr;       // rotated width (K rounded up to the rotation size), or K
-  int64_t Wp;       // max(Kr, w_in): width of the padded row in shared memory
-  double syl_h;     // Sylvester entry (only used for Sylvester sizes)
-  int vec_ok;       // 16-byte vector loads of x are legal
-  // optional row normalisation before everything else (prep_row_kernel only):
-  // 0 none, 1 LayerNorm (x - mean) * rstd * gamma + beta, 2 RMSNorm
-  // x / sqrt(mean(x^2) + eps) * gamma; rounded once to the activation dtype
-  int norm;
-  const float* gamma;
-  const float* beta;
-  float eps;
-};
 
-int num_sms();   // gemm_tc.cu
 
 // Elements of a row rotated per block-wide step (a multiple of the rotation
 // size); small enough that several rows fit in one SM's shared memory.
@@ -398,16 +374,6 @@ static cudaError_t launch_prep_t(const PrepArgs& a, cudaStream_t st) {
 
 constexpr int kPwBufDoubles = 512 + 32;   // per-warp fp64 exchange buffer (pidx(511) = 542)
 
-__device__ __forceinline__ int8_t quant1(float xv, float s, float rs) {
-  // q = rint(x / s) with the quotient correctly rounded to fp32: x * (1/s) is
-  // within 2 fp32 ulps of it, so both round to the same integer unless the
-  // product lies within 2^-21 (relative) of a half-integer; then the exact
-  // division is evaluated.  1.5 * 2^23 rounds to nearest, ties to even.
-  float y = xv * rs;
-  const float fy = fabsf(y);
-  if (fabsf(fy - (floorf(fy) + 0.5f)) <= fy * 4.8e-7f) y = __fdiv_rn(xv, s);
-  return (int8_t)max(-128, min(127, __float_as_int(y + 12582912.0f) - 0x4B400000));
-}
 
 // INTCRUSH_PREP_V1=1 routes every request to prep_quant_kernel (tests use it
 // to check the two kernels against each other).
@@ -438,30 +404,6 @@ static bool prep_v1_forced() {
 //    for the absmax, the optional prepped row / row sum and the quantisation.
 constexpr int kRowThreads = 256;
 constexpr int kRowWarps = kRowThreads / 32;
-
-template <typename T> struct MidBits;
-template <> struct MidBits<__half> {          // 10-bit mantissa: 13 fp32 bits below it
-  static constexpr uint32_t MASK = 0x1FFFu, MID = 0x1000u;
-  static constexpr float MIN_NORMAL = 6.103515625e-05f, MAX = 65504.0f;
-};
-template <> struct MidBits<__nv_bfloat16> {   // 7-bit mantissa: 16 fp32 bits below it
-  static constexpr uint32_t MASK = 0xFFFFu, MID = 0x8000u;
-  static constexpr float MIN_NORMAL = 1.1754943508e-38f, MAX = 3.38e38f;
-};
-
-// fp16-rounded (or bf16-rounded) quotient x / f given r = RN(1 / f).
-// (fp32 factor f[k] read from global memory only on the exact path)
-template <typename T>
-__device__ __forceinline__ float smoothrot_div(float x, const float* fg, int k, float r) {
-  const float y = x * r;
-  const float ay = fabsf(y);
-  const uint32_t low = __float_as_uint(y) & MidBits<T>::MASK;
-  const uint32_t d = low > MidBits<T>::MID ? low - MidBits<T>::MID : MidBits<T>::MID - low;
-  float q = y;
-  if (d <= 4u || ay < MidBits<T>::MIN_NORMAL || ay > MidBits<T>::MAX)
-    q = __fdiv_rn(x, DT<T>::to_f(DT<T>::from_f(__ldg(fg + k))));
-  return DT<T>::to_f(DT<T>::from_f(q));
-}
 
 template <typename T, int LOG2R, bool SYL, int MAXIT>
 __global__ void __launch_bounds__(kRowThreads) prep_row_kernel(const PrepArgs a, int xr_stride) {
@@ -707,8 +649,13 @@ static bool prep_row_fits(const PrepArgs& a, int log2r, size_t tsize) {
   return smem <= 200 * 1024 && !prep_v1_forced();
 }
 
+}  // namespace ic
+#include "prep_tile.cu"
+namespace ic {
+
 template <typename T>
 static cudaError_t launch_prep_dt(const PrepArgs& a, int log2r, bool syl, cudaStream_t st) {
+  if (prep_tile_fits(a, log2r, sizeof(T)) && !prep_v1_forced()) return launch_prep_tile_dt<T>(a, log2r, st);
   if (a.norm) {
     // row normalisation exists only in prep_row_kernel
     if (!prep_row_fits(a, log2r, sizeof(T))) return cudaErrorNotSupported;

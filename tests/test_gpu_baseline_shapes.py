@@ -212,3 +212,45 @@ def test_config2_layer_forward(dtype):
     yo = y.float().cpu().numpy()
     assert O.max_rel(yo[rows], r) <= 3e-2 and O.max_rel(yo[rows], r) <= 5e-3
     assert O.max_rel(yo[:, cols], c) <= 5e-3
+
+
+@pytest.mark.parametrize("kind", ["w4a8_g128", "w4a8_g128_repacked", "w4a8_per_channel", "w8a8"])
+def test_pair_tiles_match_single_cta_tiles(kind):
+    """Large GEMMs run on CTA pairs (one 256-row tile per two SMs, tcgen05
+    cta_group::2); INTCRUSH_PAIR=0 keeps one CTA per 128-row tile.  The
+    integer sums and the fp32 epilogue are the same operations in the same
+    order, so the outputs are bit-identical (fresh processes: the switch is
+    read once)."""
+    import os, subprocess, sys, tempfile
+    _dev()
+    code = (
+        "import sys; sys.path[:0] = %r\n"
+        "import conftest, numpy as np, torch, intcrush_oracle as O\n"
+        "from _pkg import load\n"
+        "rt = load('_b200_runtime')\n"
+        "kind = %r\n"
+        "M, N, K = 2500, 6400, 3072\n"   # ragged: 2500 = 13 x 192 + 4, 6400 = 25 x 256
+        "rng = np.random.default_rng(11)\n"
+        "xq = torch.from_numpy(rng.integers(-128, 128, (M, K)).astype(np.int8)).cuda()\n"
+        "int4 = kind != 'w8a8'\n"
+        "wq = rng.integers(-8, 8, (N, K)) if int4 else rng.integers(-127, 128, (N, K))\n"
+        "w = torch.from_numpy(O.pack_int4(wq.astype(np.int8)) if int4 else wq.astype(np.int8)).cuda()\n"
+        "G = 24 if kind.startswith('w4a8_g') else 1\n"
+        "rep = kind.endswith('repacked')\n"
+        "if rep: w = rt.repack_int4(w, K, 0)\n"
+        "s_w = torch.from_numpy(rng.uniform(1e-3, 2e-2, (N, G)).astype(np.float32)).cuda()\n"
+        "s_a = torch.from_numpy(rng.uniform(1e-3, 5e-2, M).astype(np.float32)).cuda()\n"
+        "b = torch.from_numpy((rng.standard_normal(N) * 0.02).astype(np.float16)).cuda()\n"
+        "y = rt.gemm_a8(xq, w, s_w, s_a, bias=b, out_dtype=torch.float16, group_size=128, repacked=rep)\n"
+        "torch.cuda.synchronize(); assert rt.device_error() == 0\n"
+        "np.save(sys.argv[1], y.cpu().numpy())\n"
+    ) % ([os.path.dirname(__file__)], kind)
+    outs = []
+    for pair in ("1", "0"):
+        f = tempfile.mktemp(suffix=".npy")
+        env = dict(os.environ, INTCRUSH_PAIR=pair)
+        r = subprocess.run([sys.executable, "-c", code, f], env=env, capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        outs.append(np.load(f))
+        os.remove(f)
+    assert np.array_equal(outs[0].view(np.uint16), outs[1].view(np.uint16))

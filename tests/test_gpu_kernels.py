@@ -80,6 +80,12 @@ def test_prep_quant_bit_exact(M, K, rot, w_in, use_perm, use_sr, use_sm):
     assert np.array_equal(s_a.cpu().numpy(), s_ref), "scales differ"
     assert np.array_equal(xq.cpu().numpy(), q_ref), "int8 activations differ"
     np.testing.assert_allclose(rs.cpu().numpy(), ref.astype(np.float64).sum(1), rtol=1e-3, atol=1e-2)
+    # quantised output alone: the 4-row tile kernel's route where it applies
+    xq2, s_a2, _, _ = rt.prep_quantize(
+        _t(x, dev), smoothrot=None if sr is None else _t(sr, dev), rot_size=rot, w_in=w_in,
+        perm=None if perm is None else _t(perm, dev), smooth=None if sm is None else _t(sm, dev))
+    assert np.array_equal(s_a2.cpu().numpy(), s_ref), "scales differ (quantised output only)"
+    assert np.array_equal(xq2.cpu().numpy(), q_ref), "int8 activations differ (quantised output only)"
 
 
 def test_prep_both_kernels_bit_identical():
@@ -427,3 +433,46 @@ def test_unpack_kernels_bit_exact():
 def test_no_device_timeouts_recorded():
     _dev()
     assert rt.device_error(clear=True) == 0
+
+
+@pytest.mark.parametrize("M,K,rot,w_in,perm,sr,sm,dt", [
+    (4096, 3072, 256, 3072, True, True, False, "f16"),
+    (37, 3000, 256, 3072, True, False, True, "f16"),
+    (100, 1000, 16, 1010, True, False, True, "bf16"),
+    (9, 4096, 64, 4096, False, True, False, "bf16"),
+    (513, 2048, 128, 2048, True, True, False, "f16"),
+    (70, 96, 32, 100, True, False, False, "f16"),
+    (1, 64, 0, 80, True, False, True, "f16"),
+    (2050, 1536, 0, 1536, False, False, False, "bf16"),
+])
+def test_prep_tile_kernel_matches_previous_kernels(M, K, rot, w_in, perm, sr, sm, dt):
+    """The 4-row tile kernel (default route for quantised output of rows of
+    <= 4096 columns, rotation 0 or 16..256) against the earlier per-row
+    kernels (INTCRUSH_PREP_TILE=0): same int8 values and scales, bit for bit
+    (fresh processes, the switch is read once)."""
+    import subprocess, sys, os, tempfile
+    _dev()
+    code = (
+        "import sys; sys.path[:0] = %r\n"
+        "import conftest, numpy as np, torch\n"
+        "from _pkg import load\n"
+        "rt = load('_b200_runtime')\n"
+        "M, K, rot, w_in, perm, sr, sm, dt = %r\n"
+        "rng = np.random.default_rng(M + K)\n"
+        "x = torch.from_numpy((rng.standard_normal((M, K)) * 3).astype(np.float32))\n"
+        "x = x.to(torch.float16 if dt == 'f16' else torch.bfloat16).cuda()\n"
+        "P = torch.from_numpy(rng.permutation(w_in).astype(np.int32)).cuda() if perm else None\n"
+        "S = torch.from_numpy(rng.uniform(0.5, 4, K).astype(np.float32)).cuda() if sr else None\n"
+        "Q = torch.from_numpy(rng.uniform(0.5, 2, w_in).astype(np.float32)).cuda() if sm else None\n"
+        "q, s, _, _ = rt.prep_quantize(x, smoothrot=S, rot_size=rot, w_in=w_in, perm=P, smooth=Q)\n"
+        "np.save(sys.argv[1], np.concatenate([q.cpu().numpy().view(np.uint8).ravel(), s.cpu().numpy().view(np.uint8)]))\n"
+    ) % ([os.path.dirname(__file__)], (M, K, rot, w_in, perm, sr, sm, dt))
+    outs = []
+    for tile in ("1", "0"):
+        f = tempfile.mktemp(suffix=".npy")
+        env = dict(os.environ, INTCRUSH_PREP_TILE=tile)
+        r = subprocess.run([sys.executable, "-c", code, f], env=env, capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        outs.append(np.load(f))
+        os.remove(f)
+    assert np.array_equal(outs[0], outs[1])
