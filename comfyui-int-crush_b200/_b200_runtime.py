@@ -418,14 +418,17 @@ def gemm_w4a16(
     K: int | None = None,
     w_layout: int = 0,
 ) -> torch.Tensor:
-    """W4A16: ``fp16(x @ fp16(q * s)^T (+ bias))`` then ``+= lr_scale * lr_mid @ lr_up^T``.
+    """W4A16: ``T(x @ W^T (+ bias))`` then ``+= lr_scale * lr_mid @ lr_up^T``,
+    T = x's dtype.  fp16: ``W = fp16(q * fp16(s))`` (the Triton unpack's
+    product); bf16: ``W = bf16(q * s)`` from the fp32 product (the PyTorch
+    path's dequantisation cast to the activation dtype).
 
     Replaces ``unpack_int4_to_float16`` + ``F.linear`` (``_ops.py:473-474``)
-    and the PyTorch INT4 path (``_ops.py:483-491``).  ``x`` must be fp16.
+    and the PyTorch INT4 path (``_ops.py:483-491``).
     """
     _need_cuda("gemm_w4a16", x, packed, scale, bias, lr_mid, lr_up, out)
-    if x.dtype != torch.float16:
-        raise TypeError(f"gemm_w4a16: activations must be float16, got {x.dtype}")
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError(f"gemm_w4a16: activations must be float16 or bfloat16, got {x.dtype}")
     x2 = x if x.stride(-1) == 1 else x.contiguous()
     M, Kx = x2.shape
     K = Kx if K is None else K
@@ -439,13 +442,15 @@ def gemm_w4a16(
     G = sc.shape[1]
     gs = int(group_size) if (G > 1 and group_size is not None) else (-(-K // G) if G > 1 else K)
     if out is None:
-        out = torch.empty((M, N), dtype=torch.float16, device=x.device)
+        out = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    elif out.dtype != x.dtype:
+        raise TypeError("gemm_w4a16: out must have x's dtype")
     b = None if bias is None else bias.contiguous()
-    mid = None if lr_mid is None else lr_mid.to(torch.float16).contiguous()
-    up = None if lr_up is None else lr_up.to(torch.float16).contiguous()
+    mid = None if lr_mid is None else lr_mid.to(x.dtype).contiguous()
+    up = None if lr_up is None else lr_up.to(x.dtype).contiguous()
     R = 0 if mid is None else mid.shape[1]
     st = L.lib().ic_gemm_w4a16(
-        _p(x2), L.IC_DTYPE_F16, M, K, x2.stride(0), _p(packed), N, packed.stride(0), int(w_layout),
+        _p(x2), _DT[x.dtype], M, K, x2.stride(0), _p(packed), N, packed.stride(0), int(w_layout),
         _p(sc), _DT[sc.dtype],
         G, gs, _p(b), _DT[b.dtype] if b is not None else 0, _p(mid), _p(up), R, float(lr_scale),
         _p(out), out.stride(0), _stream(x2))
@@ -454,30 +459,33 @@ def gemm_w4a16(
 
 
 def lowrank_down(x: torch.Tensor, down: torch.Tensor) -> torch.Tensor:
-    """``mid = fp16(x @ down^T)`` (``F.linear(x_raw, down)``, ``_ops.py:242``)."""
+    """``mid = T(x @ down^T)`` (``F.linear(x_raw, down)``, ``_ops.py:242``),
+    T = x's dtype (fp16 or bf16; other dtypes compute in fp16)."""
     _need_cuda("lowrank_down", x, down)
-    x2 = x.reshape(-1, x.shape[-1]).to(torch.float16)
+    dt = x.dtype if x.dtype in (torch.float16, torch.bfloat16) else torch.float16
+    x2 = x.reshape(-1, x.shape[-1]).to(dt)
     if x2.stride(-1) != 1:
         x2 = x2.contiguous()
-    d = down.to(torch.float16).contiguous()
+    d = down.to(dt).contiguous()
     M, K = x2.shape
     R = d.shape[0]
-    mid = torch.empty((M, R), dtype=torch.float16, device=x.device)
-    L.check(L.lib().ic_lowrank_down(_p(x2), M, K, x2.stride(0), _p(d), R, _p(mid), _stream(x2)),
-            "ic_lowrank_down")
+    mid = torch.empty((M, R), dtype=dt, device=x.device)
+    L.check(L.lib().ic_lowrank_down_ex(_p(x2), _DT[dt], M, K, x2.stride(0), _p(d), R, _p(mid), _stream(x2)),
+            "ic_lowrank_down_ex")
     return mid
 
 
 def lowrank_add(out: torch.Tensor, mid: torch.Tensor, up: torch.Tensor, scale: float) -> torch.Tensor:
-    """In place ``out = fp16(out + scale * mid @ up^T)`` (``out.addmm_``, ``_ops.py:243``)."""
+    """In place ``out = T(out + scale * mid @ up^T)`` (``out.addmm_``,
+    ``_ops.py:243``); out fp16 or bf16, rank up to 256."""
     _need_cuda("lowrank_add", out, mid, up)
-    if out.dtype != torch.float16 or out.stride(1) != 1:
-        raise TypeError("lowrank_add: out must be a row-major float16 matrix")
-    m = mid.to(torch.float16).contiguous()
-    u = up.to(torch.float16).contiguous()
+    if out.dtype not in (torch.float16, torch.bfloat16) or out.stride(1) != 1:
+        raise TypeError("lowrank_add: out must be a row-major float16 / bfloat16 matrix")
+    m = mid.to(out.dtype).contiguous()
+    u = up.to(out.dtype).contiguous()
     M, N = out.shape
-    L.check(L.lib().ic_lowrank_add(_p(out), M, N, out.stride(0), _p(m), _p(u), m.shape[1], float(scale),
-                                   _stream(out)), "ic_lowrank_add")
+    L.check(L.lib().ic_lowrank_add_ex(_p(out), _DT[out.dtype], M, N, out.stride(0), _p(m), _p(u), m.shape[1],
+                                      float(scale), _stream(out)), "ic_lowrank_add_ex")
     return out
 
 

@@ -48,8 +48,11 @@ SIGNATURES: dict[str, list] = {
     "ic_gemm_w4a16": [_P, _I, _L, _L, _L, _P, _L, _L, _I, _P, _I, _L, _L, _P, _I, _P, _P, _L, _F, _P, _L, _P],
     "ic_repack_int4": [_P, _L, _L, _L, _P, _L, _I, _P],
     "ic_lowrank_down": [_P, _L, _L, _L, _P, _L, _P, _P],
+    "ic_lowrank_down_ex": [_P, _I, _L, _L, _L, _P, _L, _P, _P],
     "ic_lowrank_add": [_P, _L, _L, _L, _P, _P, _L, _F, _P],
+    "ic_lowrank_add_ex": [_P, _I, _L, _L, _L, _P, _P, _L, _F, _P],
     "ic_unpack_int4_to_int8": [_P, _L, _L, _L, _P, _P],
+    "ic_selftest_wait_timeout": [_L, _P],
     "ic_unpack_int4_to_f16": [_P, _L, _L, _L, _P, _I, _L, _L, _P, _P],
 }
 

@@ -360,12 +360,9 @@ def make_intcrush_ops(quant_format: str, rot_size: int, use_pytorch: bool = Fals
             def _forward_int4_w4a16(self, qdata: torch.Tensor, weight: Any, bias: torch.Tensor | None,
                                     x: torch.Tensor) -> torch.Tensor:
                 """INT4 W4A16 (``_ops.py:466-481``) and the PyTorch INT4 path
-                (``:483-491``), which share their numerics: ``x_prep @
-                fp16(q * s)^T``, no bias (as in the reference)."""
-                if x.dtype != torch.float16:
-                    raise NotImplementedError(
-                        "INT-Crush B200: the W4A16 path computes in float16 (its fp16 dequantised "
-                        f"weights); got activations of dtype {x.dtype}")
+                (``:483-491``): ``x_prep @ W^T`` with the weights dequantised in
+                the activation dtype (fp16: fp16(q * s); bf16: bf16(q * s)),
+                no bias (as in the reference)."""
                 bw = self._b200_weights(weight, x.device)
                 needs_zp = bw.zp_corr is not None
                 svd = self._intcrush_L1 is not None and self._intcrush_L2 is not None
@@ -382,9 +379,9 @@ def make_intcrush_ops(quant_format: str, rot_size: int, use_pytorch: bool = Fals
                                      group_size=bw.group_size, lr_mid=mid, lr_up=up, lr_scale=scale,
                                      K=bw.K, w_layout=1 if rep is not None else 0)
                 if needs_zp:
-                    # out -= fp16(rowsum) * fp16(s*zp), one rounding (out.addmm_ of _ops.py:476-478)
-                    _rt.lowrank_add(out, _round_to(rowsum, torch.float16).half().reshape(-1, 1),
-                                    bw.zp_corr.half().reshape(-1, 1), -1.0)
+                    # out -= T(rowsum) * T(s*zp), one rounding (out.addmm_ of _ops.py:476-478)
+                    _rt.lowrank_add(out, _round_to(rowsum, x.dtype).to(x.dtype).reshape(-1, 1),
+                                    bw.zp_corr.to(x.dtype).reshape(-1, 1), -1.0)
                 if lora is not None:
                     if svd:
                         out = self._apply_residuals_svd_only(x, out, x_prep)
@@ -625,15 +622,15 @@ def _round_to(t: torch.Tensor | None, dtype: torch.dtype) -> torch.Tensor | None
 
 def _lowrank_residual(out: torch.Tensor, x2: torch.Tensor, down: torch.Tensor, up: torch.Tensor,
                       scale: float) -> torch.Tensor:
-    """``out += scale * fp16(x2 @ down^T) @ up^T`` (``F.linear`` then ``addmm_``
-    of ``_ops.py:242-243`` / ``:383-384``) on the low-rank kernels; float16
-    outputs only (the kernels' dtype)."""
-    if out.dtype != torch.float16 or down.shape[0] > 64:
-        raise NotImplementedError(
-            f"INT-Crush B200: low-rank residuals run in float16 with rank <= 64 "
-            f"(got {out.dtype}, rank {down.shape[0]})")
-    mid = _rt.lowrank_down(x2, down)
-    return _rt.lowrank_add(out, mid, up, scale)
+    """``out += scale * T(x2 @ down^T) @ up^T`` (``F.linear`` then ``addmm_``
+    of ``_ops.py:242-243`` / ``:383-384``) on the low-rank kernels for fp16 /
+    bf16 outputs up to rank 256; other output dtypes or larger ranks run the
+    reference's own two torch calls on the GPU."""
+    if out.dtype in (torch.float16, torch.bfloat16) and down.shape[0] <= 256 and out.stride(-1) == 1:
+        mid = _rt.lowrank_down(x2.to(out.dtype), down)
+        return _rt.lowrank_add(out, mid, up, scale)
+    mid = F.linear(x2.to(down.dtype), down)
+    return out.addmm_(mid.to(out.dtype), up.t().to(out.dtype), beta=1, alpha=scale)
 
 
 __all__ = ["make_intcrush_ops"]

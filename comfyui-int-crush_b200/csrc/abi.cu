@@ -14,6 +14,11 @@ namespace {
 
 thread_local char g_err[512] = "";
 
+__device__ __forceinline__ void mbar_init_for_selftest(uint64_t* bar) {
+  ic::mbar_init(bar, 1);
+  ic::fence_barrier_init();
+}
+
 int fail(int code, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
@@ -54,6 +59,30 @@ int ic_trace_read(unsigned long long* out, int clear) {
 #endif
 
 const char* ic_last_error(void) { return g_err; }
+
+// Self-test of the bounded waits: one thread waits on an mbarrier that
+// nothing arrives on, with a limit of limit_ns, so the wait runs out the way
+// a stuck pipeline's would and records IC_DEV_ERR_TIMEOUT in the device
+// error word; the kernel then returns normally.  No fault, no trap.
+__global__ void selftest_wait_kernel(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  mbar_init_for_selftest(&bar);
+  const uint64_t t0 = ic::globaltimer();
+  while (!ic::mbar_try_wait(&bar, 0)) {
+    if (ic::globaltimer() - t0 > limit_ns) {
+      ic::set_dev_error(IC_DEV_ERR_TIMEOUT);
+      break;
+    }
+  }
+}
+
+int ic_selftest_wait_timeout(int64_t limit_ns, void* stream) {
+  g_err[0] = 0;
+  if (limit_ns <= 0 || limit_ns > 100000000LL)
+    return fail(IC_ERR_ARG, "ic_selftest_wait_timeout: limit must be in (0, 0.1 s]");
+  selftest_wait_kernel<<<1, 1, 0, (cudaStream_t)stream>>>((uint64_t)limit_ns);
+  return cuda_status(cudaGetLastError(), "ic_selftest_wait_timeout launch");
+}
 
 int ic_read_device_error(int clear, int* code_out) {
   int v = 0;
@@ -295,7 +324,8 @@ int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
                   const void* bias, int bias_dtype, const void* lr_mid, const void* lr_up, int64_t R,
                   float lr_scale, void* out, int64_t ldo, void* stream) {
   g_err[0] = 0;
-  if (x_dtype != IC_DTYPE_F16) return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: x must be fp16");
+  if (x_dtype != IC_DTYPE_F16 && x_dtype != IC_DTYPE_BF16)
+    return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: x must be fp16 or bf16");
   if (M < 0 || N < 0 || K <= 0 || ldx < K || ldo < N) return fail(IC_ERR_ARG, "ic_gemm_w4a16: bad sizes");
   if (M == 0 || N == 0) return IC_OK;
   if (!x || !w || !scale || !out) return fail(IC_ERR_ARG, "ic_gemm_w4a16: NULL operand");
@@ -306,7 +336,7 @@ int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
   if (ldw < (K + 1) / 2) return fail(IC_ERR_ARG, "ic_gemm_w4a16: ldw < ceil(K/2)");
   if (w_layout != 0 && w_layout != 1) return fail(IC_ERR_ARG, "ic_gemm_w4a16: w_layout must be 0 or 1");
   if ((lr_mid == nullptr) != (lr_up == nullptr)) return fail(IC_ERR_ARG, "ic_gemm_w4a16: lr_mid and lr_up go together");
-  if (lr_mid && (R <= 0 || R > 64)) return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: low-rank R must be in [1, 64]");
+  if (lr_mid && (R <= 0 || R > 256)) return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: low-rank R must be in [1, 256]");
   const cudaStream_t st = (cudaStream_t)stream;
   static const int skinny_max = [] {
     const char* e = getenv("INTCRUSH_W4A16_SKINNY_MAX");   // tuning only
@@ -314,50 +344,61 @@ int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
   }();
   if (M <= skinny_max) {
     ic::SkinnyArgs s;
-    s.x = (const __half*)x; s.M = (int)M; s.K = (int)K; s.ldx = ldx; s.w = w; s.N = (int)N; s.ldw = ldw;
+    s.x = x; s.M = (int)M; s.K = (int)K; s.ldx = ldx; s.w = w; s.N = (int)N; s.ldw = ldw;
     s.scale = scale; s.scale_dtype = scale_dtype; s.G = (int)G; s.group_size = (int)group_size;
-    s.bias = bias; s.bias_dtype = bias_dtype; s.lr_mid = (const __half*)lr_mid; s.lr_up = (const __half*)lr_up;
-    s.R = (int)R; s.lr_scale = lr_scale; s.out = (__half*)out; s.ldo = ldo; s.repacked = w_layout;
-    return cuda_status(ic::launch_w4a16_skinny(s, st), "ic_gemm_w4a16 (small M) launch");
+    s.bias = bias; s.bias_dtype = bias_dtype; s.lr_mid = lr_mid; s.lr_up = lr_up;
+    s.R = (int)R; s.lr_scale = lr_scale; s.out = out; s.ldo = ldo; s.repacked = w_layout;
+    return cuda_status(ic::launch_w4a16_skinny(s, x_dtype, st), "ic_gemm_w4a16 (small M) launch");
   }
   if (K % 64 || ldx % 8 || !aligned16(x) || ldw % 16 || !aligned16(w))
     return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: M > 128 needs K %% 64 == 0 and 16-byte aligned rows");
   ic::GemmArgs a;
   memset(&a, 0, sizeof(a));
   a.G = (int)G; a.group_size = (int)group_size; a.w_scale = scale; a.w_scale_dtype = scale_dtype;
-  a.bias = bias; a.bias_dtype = bias_dtype; a.out = out; a.out_dtype = IC_DTYPE_F16; a.ldo = ldo;
+  a.bias = bias; a.bias_dtype = bias_dtype; a.out = out; a.out_dtype = x_dtype; a.ldo = ldo;
   a.w_repacked = w_layout;
   const char* why = "kernel launch";
-  cudaError_t e = ic::launch_gemm_w4a16_tc(x, (int)M, (int)K, ldx, w, (int)N, ldw, a, 0, st, &why);
+  cudaError_t e = ic::launch_gemm_w4a16_tc(x, x_dtype, (int)M, (int)K, ldx, w, (int)N, ldw, a, 0, st, &why);
   if (e != cudaSuccess) return cuda_status(e, why);
   if (lr_mid)
-    return cuda_status(ic::launch_lowrank_add((__half*)out, (int)M, (int)N, ldo, (const __half*)lr_mid,
-                                              (const __half*)lr_up, (int)R, lr_scale, st),
+    return cuda_status(ic::launch_lowrank_add(out, x_dtype, (int)M, (int)N, ldo, lr_mid, lr_up, (int)R, lr_scale, st),
                        "ic_gemm_w4a16 low-rank launch");
   return IC_OK;
 }
 
-int ic_lowrank_down(const void* x, int64_t M, int64_t K, int64_t ldx, const void* down, int64_t R, void* mid,
-                    void* stream) {
+int ic_lowrank_down_ex(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx, const void* down, int64_t R,
+                       void* mid, void* stream) {
   g_err[0] = 0;
+  if (dtype != IC_DTYPE_F16 && dtype != IC_DTYPE_BF16) return fail(IC_ERR_ARG, "ic_lowrank_down: dtype must be f16 or bf16");
   if (M < 0 || K <= 0 || ldx < K || R <= 0) return fail(IC_ERR_ARG, "ic_lowrank_down: bad sizes");
+  if (R > 65535) return fail(IC_ERR_UNSUPPORTED, "ic_lowrank_down: R must be < 65536");
   if (M == 0) return IC_OK;
   if (!x || !down || !mid) return fail(IC_ERR_ARG, "ic_lowrank_down: NULL operand");
-  return cuda_status(ic::launch_lowrank_down((const __half*)x, (int)M, (int)K, ldx, (const __half*)down, (int)R,
-                                             (__half*)mid, (cudaStream_t)stream),
+  return cuda_status(ic::launch_lowrank_down(x, dtype, (int)M, (int)K, ldx, down, (int)R, mid, (cudaStream_t)stream),
                      "ic_lowrank_down launch");
+}
+
+int ic_lowrank_down(const void* x, int64_t M, int64_t K, int64_t ldx, const void* down, int64_t R, void* mid,
+                    void* stream) {
+  return ic_lowrank_down_ex(x, IC_DTYPE_F16, M, K, ldx, down, R, mid, stream);
+}
+
+int ic_lowrank_add_ex(void* out, int dtype, int64_t M, int64_t N, int64_t ldo, const void* mid, const void* up,
+                      int64_t R, float scale, void* stream) {
+  g_err[0] = 0;
+  if (dtype != IC_DTYPE_F16 && dtype != IC_DTYPE_BF16) return fail(IC_ERR_ARG, "ic_lowrank_add: dtype must be f16 or bf16");
+  if (M < 0 || N < 0 || ldo < N || R <= 0) return fail(IC_ERR_ARG, "ic_lowrank_add: bad sizes");
+  if (R > 256) return fail(IC_ERR_UNSUPPORTED, "ic_lowrank_add: R must be <= 256");
+  if (M == 0 || N == 0) return IC_OK;
+  if (!out || !mid || !up) return fail(IC_ERR_ARG, "ic_lowrank_add: NULL operand");
+  return cuda_status(ic::launch_lowrank_add(out, dtype, (int)M, (int)N, ldo, mid, up, (int)R, scale,
+                                            (cudaStream_t)stream),
+                     "ic_lowrank_add launch");
 }
 
 int ic_lowrank_add(void* out, int64_t M, int64_t N, int64_t ldo, const void* mid, const void* up, int64_t R,
                    float scale, void* stream) {
-  g_err[0] = 0;
-  if (M < 0 || N < 0 || ldo < N || R <= 0) return fail(IC_ERR_ARG, "ic_lowrank_add: bad sizes");
-  if (R > 64) return fail(IC_ERR_UNSUPPORTED, "ic_lowrank_add: R must be <= 64");
-  if (M == 0 || N == 0) return IC_OK;
-  if (!out || !mid || !up) return fail(IC_ERR_ARG, "ic_lowrank_add: NULL operand");
-  return cuda_status(ic::launch_lowrank_add((__half*)out, (int)M, (int)N, ldo, (const __half*)mid,
-                                            (const __half*)up, (int)R, scale, (cudaStream_t)stream),
-                     "ic_lowrank_add launch");
+  return ic_lowrank_add_ex(out, IC_DTYPE_F16, M, N, ldo, mid, up, R, scale, stream);
 }
 
 int ic_repack_int4(const uint8_t* src, int64_t N, int64_t K, int64_t lds, uint8_t* dst, int64_t ldd, int layout,

@@ -40,7 +40,9 @@
 
 namespace ic {
 
-enum WMode : int { W_I8 = 0, W_I4 = 1, W_I4F = 2 };
+// W_I4B: W4A16 with bf16 activations (bf16(q * s) weights, kind::f16 in bf16)
+enum WMode : int { W_I8 = 0, W_I4 = 1, W_I4F = 2, W_I4B = 3 };
+template <int MODE> constexpr bool kF16Kind = (MODE == W_I4F || MODE == W_I4B);
 
 struct GemmArgs {
   int M;            // tokens
@@ -112,7 +114,7 @@ struct Cfg {
   static constexpr int THREADS = 32 * (4 + EPI);
   static constexpr int W_BYTES = kTileN * 128;                    // 16 KB
   static constexpr int X_BYTES = XROWS * 128;
-  static constexpr int P_BYTES = (MODE == W_I4) ? kTileN * 64 : (MODE == W_I4F ? kTileN * 32 : 0);
+  static constexpr int P_BYTES = (MODE == W_I4) ? kTileN * 64 : (kF16Kind<MODE> ? kTileN * 32 : 0);
   // group-scaled tiles: four accumulator buffers when they fit in TMEM, and
   // two 1 KB constant atoms (the operands of the re-arming MMA) at offset 0
   static constexpr int NBUF = (GROUPED && BN <= 128) ? 4 : ((GROUPED && BN == 160) ? 3 : 2);
@@ -131,14 +133,14 @@ struct Cfg {
   static constexpr int TMEM_COLS = TMEM_COLS_RAW <= 32 ? 32 : TMEM_COLS_RAW <= 64 ? 64
                                  : TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
   static constexpr int SMEM = OFF_BAR + 512 + 1024;               // barriers + alignment slack
-  static constexpr int KB_ELEMS = (MODE == W_I4F) ? 64 : 128;     // K elements per block
+  static constexpr int KB_ELEMS = kF16Kind<MODE> ? 64 : 128;      // K elements per block
   static_assert(EPI % 4 == 0, "epilogue warps cover the four TMEM lane quarters evenly");
   static_assert(CPT % 32 == 0 || (GROUPED && CPT % 16 == 0), "epilogue column slices of 32 (16 at the end)");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
   static_assert(S_X >= 2, "pipeline depth");
-  static_assert(!(GROUPED && MODE == W_I4F), "W4A16 folds scales into the weights");
+  static_assert(!(GROUPED && kF16Kind<MODE>), "W4A16 folds scales into the weights");
   static_assert(SMEM <= 227 * 1024, "shared memory");
-  static_assert(!PAIR || (MODE != W_I4F && BN % 32 == 0), "pair tiles: A8 kinds, BN / 2 a multiple of 16");
+  static_assert(!PAIR || (!kF16Kind<MODE> && BN % 32 == 0), "pair tiles: A8 kinds, BN / 2 a multiple of 16");
   static_assert(TMEM_COLS_RAW <= 512, "tensor memory");
 };
 
@@ -272,16 +274,26 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmArgs a) {
 }
 
 // W4A16: out[m, n] = fp16(v[j] + bias_n) (no activation scale).
+template <typename T>
 __device__ __forceinline__ void store_chunk_raw(const GemmArgs& a, const float* v, int m0, int n, bool nvalid,
                                                 float bias_n) {
-  __half* out = reinterpret_cast<__half*>(a.out);
+  T* out = reinterpret_cast<T*>(a.out);
   const int jmax = nvalid ? min(32, a.M - m0) : 0;
-  __half* p = out + (size_t)m0 * a.ldo + n;
+  T* p = out + (size_t)m0 * a.ldo + n;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    if (j < jmax) *p = __float2half_rn(v[j] + bias_n);
+    if (j < jmax) *p = DT<T>::from_f(v[j] + bias_n);
     p += a.ldo;
   }
+}
+
+// bf16(q * s) pairs from fp32 products (exact for 4-bit q and fp16-valued s);
+// nibbles in offset binary (q + 8).
+__device__ __forceinline__ uint32_t bf16_pair_q(uint32_t n0, uint32_t n1, float s) {
+  const float q0 = __uint_as_float(0x4B000000u | n0) - 8388616.0f;
+  const float q1 = __uint_as_float(0x4B000000u | n1) - 8388616.0f;
+  const __nv_bfloat162 h = __floats2bfloat162_rn(q0 * s, q1 * s);
+  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 }  // namespace ic
@@ -431,7 +443,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && (!PAIR || leader)) {
       constexpr int MM = PAIR ? 2 * kTileN : kTileN;
-      const uint32_t idesc = (MODE == W_I4F) ? idesc_f16(MM, BN, false) : idesc_i8(MM, BN);
+      const uint32_t idesc = kF16Kind<MODE> ? idesc_f16(MM, BN, MODE == W_I4B) : idesc_i8(MM, BN);
       // GROUPED: the re-arming MMA (kind::f16, K = 16, accumulate off) writes
       // 1.5 * 2^23 as fp32 into every element of the buffer; the group's
       // kind::i8 MMAs then add the int32 partial onto those bits.  SBO = 0 makes
@@ -478,7 +490,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const uint32_t acc = GROUPED ? 1u : ((kb > kb0 || k > 0) ? 1u : 0u);
-              if constexpr (MODE == W_I4F) mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, acc);
+              if constexpr (kF16Kind<MODE>) mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, acc);
               else if constexpr (PAIR) mma_i8_2(d, adesc + 2 * k, bdesc + 2 * k, idesc, acc);
               else mma_i8(d, adesc + 2 * k, bdesc + 2 * k, idesc, acc);
             }
@@ -583,6 +595,43 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
                 expand_i4_i8(p.w, o1.z, o1.w);
                 *reinterpret_cast<uint4*>(W + sw128_offset(r, 2 * c)) = o0;
                 *reinterpret_cast<uint4*>(W + sw128_offset(r, 2 * c + 1)) = o1;
+              }
+            }
+          } else if constexpr (MODE == W_I4B) {
+            const int g = (a.G > 1) ? (kb * 64) / a.group_size : 0;
+            const int c = lane & 1;
+            float sf[8];
+            uint4 pk[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = i * 16 + (lane >> 1);
+              const int n = n_blk * kTileN + r;
+              sf[i] = 0.f;
+              if (n < a.N) {
+                const size_t si = (size_t)n * a.G + g;
+                sf[i] = (a.w_scale_dtype == IC_DTYPE_F16) ? __half2float(reinterpret_cast<const __half*>(a.w_scale)[si])
+                                                          : reinterpret_cast<const float*>(a.w_scale)[si];
+              }
+              pk[i] = *reinterpret_cast<const uint4*>(P + r * 32 + c * 16);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = i * 16 + (lane >> 1);
+              const uint32_t pw[4] = {pk[i].x, pk[i].y, pk[i].z, pk[i].w};
+#pragma unroll
+              for (int w = 0; w < 4; ++w) {
+                uint4 o;
+                uint32_t* op = &o.x;
+#pragma unroll
+                for (int t2 = 0; t2 < 4; ++t2) {
+                  if (rp) {   // layout 1: nibbles (t, t + 4) = (k_2t, k_2t+1) + 8
+                    op[t2] = bf16_pair_q((pw[w] >> (4 * t2)) & 0xFu, (pw[w] >> (4 * t2 + 16)) & 0xFu, sf[i]);
+                  } else {    // reference packing: byte t = q[2t] | q[2t+1] << 4
+                    const uint32_t ob = pw[w] ^ 0x88888888u;
+                    op[t2] = bf16_pair_q((ob >> (8 * t2)) & 0xFu, (ob >> (8 * t2 + 4)) & 0xFu, sf[i]);
+                  }
+                }
+                *reinterpret_cast<uint4*>(W + sw128_offset(r, 4 * c + w)) = o;
               }
             }
           } else {
@@ -740,7 +789,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         }
       } else {
         const int b = uc % NB;
-        const float sw = (MODE == W_I4F) ? 1.f : (nvalid ? __ldg(&a.s_w[n]) * wmul : 0.f);
+        const float sw = kF16Kind<MODE> ? 1.f : (nvalid ? __ldg(&a.s_w[n]) * wmul : 0.f);
         if (!acc_wait(b, (uint32_t)(uc / NB) & 1u)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll 1
@@ -752,8 +801,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            v[j] = (MODE == W_I4F) ? __uint_as_float(r[j]) : (float)(int)r[j] * sw;
-          if constexpr (MODE == W_I4F) store_chunk_raw(a, v, mbase + 32 * c, n, nvalid, bias_n);
+            v[j] = kF16Kind<MODE> ? __uint_as_float(r[j]) : (float)(int)r[j] * sw;
+          if constexpr (MODE == W_I4F) store_chunk_raw<__half>(a, v, mbase + 32 * c, n, nvalid, bias_n);
+          else if constexpr (MODE == W_I4B) store_chunk_raw<__nv_bfloat16>(a, v, mbase + 32 * c, n, nvalid, bias_n);
           else if (a.splits > 1) store_partial(a, v, split, mbase + 32 * c, n, nvalid, lane);
           else store_chunk(a, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane);
         }
@@ -1018,12 +1068,13 @@ cudaError_t launch_gemm_a8(const int8_t* xq, int M, int K, long long ldq, const 
 }
 
 // Entry used by ic_gemm_w4a16 for M above the skinny-kernel range.
-cudaError_t launch_gemm_w4a16_tc(const void* x, int M, int K, long long ldx, const uint8_t* w, int N,
+cudaError_t launch_gemm_w4a16_tc(const void* x, int x_dtype, int M, int K, long long ldx, const uint8_t* w, int N,
                                  long long ldw, GemmArgs a, int force_bn, cudaStream_t st, const char** why) {
   CUtensorMap tx, tw;
   const int bn = force_bn ? force_bn : pick_bn(M, N, false);
-  if (!make_tmap(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, (uint64_t)K, (uint64_t)M, (uint64_t)ldx * 2, 64,
-                 (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B)) {
+  const bool bf = x_dtype == IC_DTYPE_BF16;
+  if (!make_tmap(&tx, bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, (uint64_t)K,
+                 (uint64_t)M, (uint64_t)ldx * 2, 64, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B)) {
     *why = "cuTensorMapEncodeTiled failed for the activation operand";
     return cudaErrorInvalidValue;
   }
@@ -1037,7 +1088,7 @@ cudaError_t launch_gemm_w4a16_tc(const void* x, int M, int K, long long ldx, con
   a.n_tiles = (N + kTileN - 1) / kTileN;
   a.splits = 1;
   a.kb_per_unit = a.num_kb;
-  return dispatch_bn<W_I4F, false>(bn, tw, tx, a, st);
+  return bf ? dispatch_bn<W_I4B, false>(bn, tw, tx, a, st) : dispatch_bn<W_I4F, false>(bn, tw, tx, a, st);
 }
 
 }  // namespace ic

@@ -16,6 +16,8 @@
 // reduced in a fixed order in shared memory (deterministic).
 #include "ic_common.cuh"
 
+#include <type_traits>
+
 namespace ic {
 
 constexpr int kSkinnyWarps = 8;
@@ -38,22 +40,47 @@ __device__ __forceinline__ uint32_t r16pair_f16(uint32_t v, int t, __half2 s2) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// bf16 weights: bf16(q * s) from the fp32 product (exact for a 4-bit q and
+// an fp16-valued s), the reference's PyTorch dequantisation followed by its
+// cast to the activation dtype (quant_layout.py:81-87, _ops.py:483-491).
+// n0, n1: offset-binary nibbles (q + 8) of k and k + 1.
+__device__ __forceinline__ uint32_t pair_bf16(uint32_t n0, uint32_t n1, float s) {
+  const float q0 = __uint_as_float(0x4B000000u | n0) - 8388616.0f;   // (2^23 + n) - (2^23 + 8)
+  const float q1 = __uint_as_float(0x4B000000u | n1) - 8388616.0f;
+  const __nv_bfloat162 h = __floats2bfloat162_rn(q0 * s, q1 * s);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t i4pair_bf16(uint32_t xo, uint32_t yo, int i, float s) {
+  return pair_bf16((xo >> (8 * i)) & 0xFu, (yo >> (8 * i)) & 0xFu, s);
+}
+__device__ __forceinline__ uint32_t r16pair_bf16(uint32_t v, int t, float s) {
+  return pair_bf16((v >> (4 * t)) & 0xFu, (v >> (4 * t + 16)) & 0xFu, s);
+}
+
+template <typename T>
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  if constexpr (std::is_same<T, __half>::value)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 struct SkinnyArgs {
-  const __half* x; int M, K; long long ldx;
+  const void* x; int M, K; long long ldx;     // activations in the activation dtype (fp16 / bf16)
   const uint8_t* w; int N; long long ldw;
   const void* scale; int scale_dtype; int G, group_size;
   const void* bias; int bias_dtype;
-  const __half* lr_mid; const __half* lr_up; int R; float lr_scale;
-  __half* out; long long ldo;
+  const void* lr_mid; const void* lr_up; int R; float lr_scale;   // activation dtype
+  void* out; long long ldo;                   // activation dtype
   int repacked;     // weights in ic_repack_int4 layout 1
 };
 
@@ -77,16 +104,24 @@ __device__ __forceinline__ __half load_scale(const SkinnyArgs& a, int n, int g) 
   return a.scale_dtype == IC_DTYPE_F16 ? reinterpret_cast<const __half*>(a.scale)[i]
                                        : __float2half_rn(reinterpret_cast<const float*>(a.scale)[i]);
 }
+__device__ __forceinline__ float load_scale_f(const SkinnyArgs& a, int n, int g) {
+  if (n >= a.N) return 0.f;
+  const size_t i = (size_t)n * a.G + g;
+  return a.scale_dtype == IC_DTYPE_F16 ? __half2float(reinterpret_cast<const __half*>(a.scale)[i])
+                                       : reinterpret_cast<const float*>(a.scale)[i];
+}
 
 // 32 activations of token m at k in [k0, k0 + 32), zero past K or M.
+template <typename T>
 __device__ __forceinline__ void load_x32(const SkinnyArgs& a, int m, long long k0, uint32_t (&w)[16]) {
   if (m >= a.M) {   // token slot past M: zeros, no loads
 #pragma unroll
     for (int i = 0; i < 16; ++i) w[i] = 0u;
     return;
   }
+  const T* x = reinterpret_cast<const T*>(a.x);
   if (k0 + 32 <= a.K && ((a.ldx & 7) == 0)) {
-    const uint4* p = reinterpret_cast<const uint4*>(a.x + (long long)m * a.ldx + k0);
+    const uint4* p = reinterpret_cast<const uint4*>(x + (long long)m * a.ldx + k0);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       uint4 v = __ldg(p + i);
@@ -94,16 +129,17 @@ __device__ __forceinline__ void load_x32(const SkinnyArgs& a, int m, long long k
     }
     return;
   }
-  __half h[32];
+  T h[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i)
-    h[i] = (m < a.M && k0 + i < a.K) ? a.x[(long long)m * a.ldx + k0 + i] : __float2half_rn(0.f);
+    h[i] = (m < a.M && k0 + i < a.K) ? x[(long long)m * a.ldx + k0 + i] : DT<T>::from_f(0.f);
 #pragma unroll
   for (int i = 0; i < 16; ++i) w[i] = *reinterpret_cast<uint32_t*>(&h[2 * i]);
 }
 
-template <int TT>
+template <int TT, typename T>
 __global__ void __launch_bounds__(32 * kSkinnyWarps, 2) w4a16_skinny_kernel(const SkinnyArgs a) {
+  constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
   __shared__ float red[kSkinnyWarps][16][8 * TT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -119,7 +155,8 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps, 2) w4a16_skinny_kernel(cons
   constexpr int PF = (TT >= 4) ? 2 : 4;
   for (int kb0 = warp; kb0 < nkb; kb0 += kSkinnyWarps * PF) {
     uint4 pa[PF], pb[PF];
-    __half2 sa[PF], sb[PF];
+    __half2 sa[PF], sb[PF];   // fp16 path: the scale as half2
+    float fa[PF], fb[PF];     // bf16 path: the scale in fp32
 #pragma unroll
     for (int j = 0; j < PF; ++j) {
       const int kb = kb0 + kSkinnyWarps * j;
@@ -127,11 +164,17 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps, 2) w4a16_skinny_kernel(cons
         pa[j] = load_packed16(a, n0 + g, kb, t);
         pb[j] = load_packed16(a, n0 + g + 8, kb, t);
         const int grp = (a.G > 1) ? (kb * 128) / a.group_size : 0;
-        sa[j] = __half2half2(load_scale(a, n0 + g, grp));
-        sb[j] = __half2half2(load_scale(a, n0 + g + 8, grp));
+        if constexpr (BF) {
+          fa[j] = load_scale_f(a, n0 + g, grp);
+          fb[j] = load_scale_f(a, n0 + g + 8, grp);
+        } else {
+          sa[j] = __half2half2(load_scale(a, n0 + g, grp));
+          sb[j] = __half2half2(load_scale(a, n0 + g + 8, grp));
+        }
       } else {
         pa[j] = pb[j] = make_uint4(0u, 0u, 0u, 0u);
         sa[j] = sb[j] = __half2half2(__float2half_rn(0.f));
+        fa[j] = fb[j] = 0.f;
       }
     }
 #pragma unroll
@@ -140,7 +183,7 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps, 2) w4a16_skinny_kernel(cons
       if (kb >= nkb) break;
       uint32_t xw[TT][16];
 #pragma unroll
-      for (int i = 0; i < TT; ++i) load_x32(a, m0 + i * 8 + g, (long long)kb * 128 + 32 * t, xw[i]);
+      for (int i = 0; i < TT; ++i) load_x32<T>(a, m0 + i * 8 + g, (long long)kb * 128 + 32 * t, xw[i]);
       const uint32_t wa[4] = {pa[j].x, pa[j].y, pa[j].z, pa[j].w};
       const uint32_t wb[4] = {pb[j].x, pb[j].y, pb[j].z, pb[j].w};
 #pragma unroll
@@ -152,7 +195,19 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps, 2) w4a16_skinny_kernel(cons
         for (int h = 0; h < 2; ++h) {   // MMA step s = 2w + h uses k pairs 2h, 2h+1 of word w
           const int s = 2 * w + h;
           uint32_t a0, a1, a2, a3;
-          if (a.repacked) {
+          if constexpr (BF) {
+            if (a.repacked) {
+              a0 = r16pair_bf16(wa[w], 2 * h, fa[j]);
+              a2 = r16pair_bf16(wa[w], 2 * h + 1, fa[j]);
+              a1 = r16pair_bf16(wb[w], 2 * h, fb[j]);
+              a3 = r16pair_bf16(wb[w], 2 * h + 1, fb[j]);
+            } else {
+              a0 = i4pair_bf16(xa, ya, 2 * h, fa[j]);
+              a2 = i4pair_bf16(xa, ya, 2 * h + 1, fa[j]);
+              a1 = i4pair_bf16(xb, yb, 2 * h, fb[j]);
+              a3 = i4pair_bf16(xb, yb, 2 * h + 1, fb[j]);
+            }
+          } else if (a.repacked) {
             a0 = r16pair_f16(wa[w], 2 * h, sa[j]);
             a2 = r16pair_f16(wa[w], 2 * h + 1, sa[j]);
             a1 = r16pair_f16(wb[w], 2 * h, sb[j]);
@@ -164,7 +219,7 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps, 2) w4a16_skinny_kernel(cons
             a3 = i4pair_f16(xb, yb, 2 * h + 1, sb[j]);
           }
 #pragma unroll
-          for (int i = 0; i < TT; ++i) mma_16816(d[i], a0, a1, a2, a3, xw[i][2 * s], xw[i][2 * s + 1]);
+          for (int i = 0; i < TT; ++i) mma_16816<T>(d[i], a0, a1, a2, a3, xw[i][2 * s], xw[i][2 * s + 1]);
         }
       }
     }
@@ -185,40 +240,49 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps, 2) w4a16_skinny_kernel(cons
 #pragma unroll
     for (int w = 0; w < kSkinnyWarps; ++w) v += red[w][r][ml];
     if (a.bias) v += load_any(a.bias, a.bias_dtype, n);
-    __half o16 = __float2half_rn(v);
+    T ov = DT<T>::from_f(v);
     if (a.lr_mid) {
+      const T* mid = reinterpret_cast<const T*>(a.lr_mid);
+      const T* up = reinterpret_cast<const T*>(a.lr_up);
       float l = 0.f;
 #pragma unroll 8
       for (int j = 0; j < a.R; ++j)
-        l = fmaf(__half2float(a.lr_mid[(long long)m * a.R + j]), __half2float(a.lr_up[(long long)n * a.R + j]), l);
-      o16 = __float2half_rn(__half2float(o16) + a.lr_scale * l);
+        l = fmaf(DT<T>::to_f(mid[(long long)m * a.R + j]), DT<T>::to_f(up[(long long)n * a.R + j]), l);
+      ov = DT<T>::from_f(DT<T>::to_f(ov) + a.lr_scale * l);
     }
-    a.out[(long long)m * a.ldo + n] = o16;
+    reinterpret_cast<T*>(a.out)[(long long)m * a.ldo + n] = ov;
   }
 }
 
-cudaError_t launch_w4a16_skinny(const SkinnyArgs& a, cudaStream_t st) {
+template <typename T>
+static cudaError_t launch_w4a16_skinny_t(const SkinnyArgs& a, cudaStream_t st) {
   // up to 32 tokens per CTA row of the grid; more tokens add CTA rows, each
   // streaming the (L2-resident) weights again
   const dim3 grid((a.N + 15) / 16, (a.M + 31) / 32);
-  if (a.M <= 8) w4a16_skinny_kernel<1><<<grid, 32 * kSkinnyWarps, 0, st>>>(a);
-  else if (a.M <= 16) w4a16_skinny_kernel<2><<<grid, 32 * kSkinnyWarps, 0, st>>>(a);
-  else w4a16_skinny_kernel<4><<<grid, 32 * kSkinnyWarps, 0, st>>>(a);
+  if (a.M <= 8) w4a16_skinny_kernel<1, T><<<grid, 32 * kSkinnyWarps, 0, st>>>(a);
+  else if (a.M <= 16) w4a16_skinny_kernel<2, T><<<grid, 32 * kSkinnyWarps, 0, st>>>(a);
+  else w4a16_skinny_kernel<4, T><<<grid, 32 * kSkinnyWarps, 0, st>>>(a);
   return cudaGetLastError();
 }
 
+cudaError_t launch_w4a16_skinny(const SkinnyArgs& a, int x_dtype, cudaStream_t st) {
+  return x_dtype == IC_DTYPE_BF16 ? launch_w4a16_skinny_t<__nv_bfloat16>(a, st) : launch_w4a16_skinny_t<__half>(a, st);
+}
+
 // ------------------------------------------------------------ low rank
-// mid[m, r] = fp16(sum_k x[m, k] * down[r, k]) with fp32 accumulation.
-// One CTA per (rank r, tile of 8 tokens): each thread takes 8-value slices
-// of K (16-byte loads of the down row and of the tile's token rows) and the
-// CTA reduces its partial sums in a fixed order (deterministic).
+// mid[m, r] = T(sum_k x[m, k] * down[r, k]) with fp32 accumulation, T the
+// activation dtype (F.linear(x_raw, down), _ops.py:242).  One CTA per (rank
+// r, tile of 8 tokens): each thread takes 8-value slices of K (16-byte loads
+// of the down row and of the tile's token rows) and the CTA reduces its
+// partial sums in a fixed order (deterministic).
 constexpr int kLrTok = 8;
-__global__ void __launch_bounds__(128) lowrank_down_kernel(const __half* x, int M, int K, long long ldx,
-                                                           const __half* down, int R, __half* mid) {
+template <typename T>
+__global__ void __launch_bounds__(128) lowrank_down_kernel(const T* x, int M, int K, long long ldx,
+                                                           const T* down, int R, T* mid) {
   __shared__ float red[4][kLrTok];
   const int r = blockIdx.x, m0 = blockIdx.y * kLrTok;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const __half* dr = down + (long long)r * K;
+  const T* dr = down + (long long)r * K;
   float acc[kLrTok];
 #pragma unroll
   for (int i = 0; i < kLrTok; ++i) acc[i] = 0.f;
@@ -227,25 +291,24 @@ __global__ void __launch_bounds__(128) lowrank_down_kernel(const __half* x, int 
   if (vec) {
     for (int c = threadIdx.x; c < K / 8; c += blockDim.x) {
       const uint4 dv = __ldg(reinterpret_cast<const uint4*>(dr) + c);
-      const __half2* d2 = reinterpret_cast<const __half2*>(&dv);
+      const T* d8 = reinterpret_cast<const T*>(&dv);
 #pragma unroll
       for (int i = 0; i < kLrTok; ++i) {
         if (m0 + i >= M) break;
         const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + (long long)(m0 + i) * ldx) + c);
-        const __half2* x2 = reinterpret_cast<const __half2*>(&xv);
+        const T* x8 = reinterpret_cast<const T*>(&xv);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 a = __half22float2(x2[j]), b = __half22float2(d2[j]);
-          acc[i] = fmaf(a.x, b.x, fmaf(a.y, b.y, acc[i]));
-        }
+        for (int j = 0; j < 8; j += 2)
+          acc[i] = fmaf(DT<T>::to_f(x8[j]), DT<T>::to_f(d8[j]),
+                        fmaf(DT<T>::to_f(x8[j + 1]), DT<T>::to_f(d8[j + 1]), acc[i]));
       }
     }
   } else {
     for (int k = threadIdx.x; k < K; k += blockDim.x) {
-      const float dv = __half2float(dr[k]);
+      const float dv = DT<T>::to_f(dr[k]);
 #pragma unroll
       for (int i = 0; i < kLrTok; ++i)
-        if (m0 + i < M) acc[i] = fmaf(__half2float(x[(long long)(m0 + i) * ldx + k]), dv, acc[i]);
+        if (m0 + i < M) acc[i] = fmaf(DT<T>::to_f(x[(long long)(m0 + i) * ldx + k]), dv, acc[i]);
     }
   }
 #pragma unroll
@@ -261,47 +324,71 @@ __global__ void __launch_bounds__(128) lowrank_down_kernel(const __half* x, int 
   if (threadIdx.x < kLrTok && m0 + (int)threadIdx.x < M) {
     const int i = threadIdx.x;
     const float v = (red[0][i] + red[1][i]) + (red[2][i] + red[3][i]);
-    mid[(long long)(m0 + i) * R + r] = __float2half_rn(v);
+    mid[(long long)(m0 + i) * R + r] = DT<T>::from_f(v);
   }
 }
 
-cudaError_t launch_lowrank_down(const __half* x, int M, int K, long long ldx, const __half* down, int R,
-                                __half* mid, cudaStream_t st) {
+cudaError_t launch_lowrank_down(const void* x, int dtype, int M, int K, long long ldx, const void* down, int R,
+                                void* mid, cudaStream_t st) {
   if (M == 0) return cudaSuccess;
   const dim3 grid(R, (M + kLrTok - 1) / kLrTok);
-  lowrank_down_kernel<<<grid, 128, 0, st>>>(x, M, K, ldx, down, R, mid);
+  if (dtype == IC_DTYPE_BF16)
+    lowrank_down_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>((const __nv_bfloat16*)x, M, K, ldx,
+                                                             (const __nv_bfloat16*)down, R, (__nv_bfloat16*)mid);
+  else
+    lowrank_down_kernel<__half><<<grid, 128, 0, st>>>((const __half*)x, M, K, ldx, (const __half*)down, R,
+                                                      (__half*)mid);
   return cudaGetLastError();
 }
 
-// out[m, n] = fp16(out[m, n] + scale * sum_r mid[m, r] * up[n, r]); R <= 64.
-__global__ void __launch_bounds__(256) lowrank_add_kernel(__half* out, int M, int N, long long ldo,
-                                                          const __half* mid, const __half* up, int R,
-                                                          float scale) {
+// out[m, n] = T(out[m, n] + scale * sum_r mid[m, r] * up[n, r]) (out.addmm_,
+// _ops.py:243): fp32 sums over the rank in chunks of 64 (R <= 256).
+template <typename T>
+__global__ void __launch_bounds__(256) lowrank_add_kernel(T* out, int M, int N, long long ldo, const T* mid,
+                                                          const T* up, int R, float scale) {
   __shared__ float ms[16][64];
   const int m0 = blockIdx.y * 16;
-  for (int i = threadIdx.x; i < 16 * 64; i += 256) {
-    const int mm = i / 64, r = i % 64;
-    ms[mm][r] = (m0 + mm < M && r < R) ? __half2float(mid[(long long)(m0 + mm) * R + r]) : 0.f;
-  }
-  __syncthreads();
   const int n = blockIdx.x * 256 + threadIdx.x;
+  float l[16];
+#pragma unroll
+  for (int mm = 0; mm < 16; ++mm) l[mm] = 0.f;
+  for (int r0 = 0; r0 < R; r0 += 64) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+      const int mm = i / 64, r = r0 + i % 64;
+      ms[mm][i % 64] = (m0 + mm < M && r < R) ? DT<T>::to_f(mid[(long long)(m0 + mm) * R + r]) : 0.f;
+    }
+    __syncthreads();
+    if (n < N) {
+      float u[64];
+#pragma unroll
+      for (int r = 0; r < 64; ++r) u[r] = (r0 + r < R) ? DT<T>::to_f(up[(long long)n * R + r0 + r]) : 0.f;
+#pragma unroll
+      for (int mm = 0; mm < 16; ++mm) {
+#pragma unroll
+        for (int r = 0; r < 64; ++r) l[mm] = fmaf(ms[mm][r], u[r], l[mm]);
+      }
+    }
+  }
   if (n >= N) return;
-  float u[64];
 #pragma unroll
-  for (int r = 0; r < 64; ++r) u[r] = (r < R) ? __half2float(up[(long long)n * R + r]) : 0.f;
-  for (int mm = 0; mm < 16 && m0 + mm < M; ++mm) {
-    float l = 0.f;
-#pragma unroll
-    for (int r = 0; r < 64; ++r) l = fmaf(ms[mm][r], u[r], l);
-    __half* o = out + (long long)(m0 + mm) * ldo + n;
-    *o = __float2half_rn(__half2float(*o) + scale * l);
+  for (int mm = 0; mm < 16; ++mm) {
+    if (m0 + mm >= M) break;
+    T* o = out + (long long)(m0 + mm) * ldo + n;
+    *o = DT<T>::from_f(DT<T>::to_f(*o) + scale * l[mm]);
   }
 }
 
-cudaError_t launch_lowrank_add(__half* out, int M, int N, long long ldo, const __half* mid, const __half* up,
+cudaError_t launch_lowrank_add(void* out, int dtype, int M, int N, long long ldo, const void* mid, const void* up,
                                int R, float scale, cudaStream_t st) {
   const dim3 grid((N + 255) / 256, (M + 15) / 16);
-  lowrank_add_kernel<<<grid, 256, 0, st>>>(out, M, N, ldo, mid, up, R, scale);
+  if (dtype == IC_DTYPE_BF16)
+    lowrank_add_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((__nv_bfloat16*)out, M, N, ldo,
+                                                            (const __nv_bfloat16*)mid, (const __nv_bfloat16*)up, R,
+                                                            scale);
+  else
+    lowrank_add_kernel<__half><<<grid, 256, 0, st>>>((__half*)out, M, N, ldo, (const __half*)mid,
+                                                     (const __half*)up, R, scale);
   return cudaGetLastError();
 }
 

@@ -173,23 +173,27 @@ int ic_gemm_a8_splitk_noalloc(const int8_t* xq, int64_t M, int64_t K, int64_t ld
                               int splits, void* stream);
 
 /*
- * (a4) W4A16: out = x @ dequant(w)^T with dequant(w)[n,k] = fp16(q[n,k] *
- * s[n, k // group_size]), fp32 accumulation, fused bias and low-rank term
- *   out = fp16(fp16(x @ W^T + bias) + lr_scale * lr_mid @ lr_up^T)
- * (the second rounding reproduces the reference's separate addmm_).
+ * (a4) W4A16: out = x @ dequant(w)^T with fp32 accumulation, fused bias and
+ * low-rank term
+ *   out = T(T(x @ W^T + bias) + lr_scale * lr_mid @ lr_up^T)
+ * (the second rounding reproduces the reference's separate addmm_), T the
+ * activation dtype.  fp16: dequant(w)[n,k] = fp16(q[n,k] * fp16(s[n, g])),
+ * the Triton unpack's product (kernels/triton_int4_unpack.py:48-56); bf16:
+ * bf16(q[n,k] * s[n, g]) from the fp32 product, the PyTorch path's
+ * dequantisation cast to the activation dtype (quant_layout.py:81-87,
+ * _ops.py:483-491).
  *
  * Replaces unpack_int4_to_float16 (kernels/triton_int4_unpack.py:62-88) +
  * F.linear (_ops.py:473-474), the PyTorch INT4 path (_ops.py:483-491) and the
  * LoRA residual (_ops.py:236-244) for standard LoRA.
  *
- *   x      [M, K] fp16 (x_dtype must be IC_DTYPE_F16), row stride ldx
+ *   x      [M, K] fp16 or bf16 (x_dtype), row stride ldx
  *   w      uint8 [N, ceil(K/2)], row stride ldw bytes; w_layout 0 = the
  *          reference packing, 1 = ic_repack_int4 layout 1 (faster)
- *   scale  [N, G] in scale_dtype (f16 or f32; cast to fp16 like the
- *          reference), group_size % 128 == 0 when G > 1
+ *   scale  [N, G] in scale_dtype (f16 or f32), group_size % 128 == 0 when G > 1
  *   bias   [N] or NULL
- *   lr_mid [M, R] fp16, lr_up [N, R] fp16 (R <= 64) or NULL
- *   out    [M, N] fp16, row stride ldo
+ *   lr_mid [M, R], lr_up [N, R] in x_dtype (R <= 256) or NULL
+ *   out    [M, N] in x_dtype, row stride ldo
  */
 int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
                   const uint8_t* w, int64_t N, int64_t ldw, int w_layout,
@@ -198,16 +202,30 @@ int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
                   const void* lr_mid, const void* lr_up, int64_t R, float lr_scale,
                   void* out, int64_t ldo, void* stream);
 
-/* Low-rank "down" projection mid = fp16(x @ down^T) (_ops.py:242, F.linear
- * in fp16): x [M, K] fp16 (ldx), down [R, K] fp16, mid [M, R] fp16. */
+/* Low-rank "down" projection mid = T(x @ down^T) with fp32 accumulation
+ * (_ops.py:242, F.linear in the activation dtype T): x [M, K] (ldx),
+ * down [R, K], mid [M, R], all in dtype (IC_DTYPE_F16 or IC_DTYPE_BF16). */
+int ic_lowrank_down_ex(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx, const void* down,
+                       int64_t R, void* mid, void* stream);
+/* ic_lowrank_down_ex with dtype IC_DTYPE_F16. */
 int ic_lowrank_down(const void* x, int64_t M, int64_t K, int64_t ldx, const void* down,
                     int64_t R, void* mid, void* stream);
 
-/* In-place low-rank residual out = fp16(out + scale * mid @ up^T)
- * (out.addmm_ of _ops.py:243 / :384): out [M, N] fp16 (ldo),
- * mid [M, R] fp16, up [N, R] fp16. */
+/* In-place low-rank residual out = T(out + scale * mid @ up^T), fp32 sums
+ * (out.addmm_ of _ops.py:243 / :384): out [M, N] (ldo), mid [M, R],
+ * up [N, R], all in dtype (f16 or bf16); R <= 256. */
+int ic_lowrank_add_ex(void* out, int dtype, int64_t M, int64_t N, int64_t ldo, const void* mid,
+                      const void* up, int64_t R, float scale, void* stream);
+/* ic_lowrank_add_ex with dtype IC_DTYPE_F16. */
 int ic_lowrank_add(void* out, int64_t M, int64_t N, int64_t ldo, const void* mid,
                    const void* up, int64_t R, float scale, void* stream);
+
+/* Self-test of the kernels' bounded waits (no counterpart in the
+ * reference; failure detection): launches one thread that waits on an
+ * mbarrier nothing arrives on, gives up after limit_ns (<= 0.1 s), records
+ * IC_DEV_ERR_TIMEOUT in the device error word (ic_read_device_error) and
+ * returns.  The context stays usable. */
+int ic_selftest_wait_timeout(int64_t limit_ns, void* stream);
 
 /* Load-time weight repack.  The reference's packing (_quant_utils.py:
  * 170-182) stays the input format; this permutes the nibbles of each 4-byte

@@ -39,10 +39,12 @@ def test_version():
      L.IC_ERR_ARG),
     (lambda l: l.ic_prep_quant(ctypes.c_void_p(16), 0, 4, 64, 64, None, 48, 64, None, None, None, 0, None, None,
                                None, None), L.IC_ERR_ARG),
-    (lambda l: l.ic_gemm_w4a16(None, 1, 4, 64, 64, None, 8, 32, 0, None, 0, 1, 64, None, 0, None, None, 0, 1.0,
+    (lambda l: l.ic_gemm_w4a16(None, 2, 4, 64, 64, None, 8, 32, 0, None, 0, 1, 64, None, 0, None, None, 0, 1.0,
                                None, 8, None), L.IC_ERR_UNSUPPORTED),
     (lambda l: l.ic_repack_int4(None, 4, 64, 32, None, 32, 5, None), L.IC_ERR_ARG),
-    (lambda l: l.ic_lowrank_add(None, 4, 8, 8, None, None, 128, 1.0, None), L.IC_ERR_UNSUPPORTED),
+    (lambda l: l.ic_lowrank_add(None, 4, 8, 8, None, None, 512, 1.0, None), L.IC_ERR_UNSUPPORTED),
+    (lambda l: l.ic_lowrank_add_ex(None, 2, 4, 8, 8, None, None, 16, 1.0, None), L.IC_ERR_ARG),
+    (lambda l: l.ic_lowrank_down_ex(None, 2, 4, 8, 8, None, 16, None, None), L.IC_ERR_ARG),
 ])
 def test_argument_validation_without_gpu(call, code):
     lib = L.lib()

@@ -221,3 +221,24 @@ def test_lora_attach_and_clear(monkeypatch):
     assert (attached, total) == (1, 2)
     assert lin._intcrush_lora_strength == 0.5 and isinstance(lin._intcrush_adapter, Adapter)
     assert lora.clear_intcrush_lora(model) == 1 and lin._intcrush_adapter is None
+
+
+def test_torch_custom_ops_registered_with_fake_kernels():
+    """The kernels are ``torch.library`` custom ops (``intcrush_b200::*``) with
+    fake implementations: shapes and dtypes propagate on meta tensors
+    without a GPU (what torch.compile / export trace through)."""
+    import torch
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    load("_torch_ops")
+    ops = torch.ops.intcrush_b200
+    with FakeTensorMode():
+        x = torch.empty(37, 3000, dtype=torch.float16)
+        xq, s_a = ops.prep_quantize(x, None, None, None, 256, 3072)
+        assert xq.shape == (37, 3072) and xq.dtype == torch.int8 and s_a.shape == (37,)
+        w = torch.empty(640, 1536, dtype=torch.uint8)
+        s_w = torch.empty(640, 24)
+        y = ops.gemm_a8(xq, w, s_w, s_a, None, 1, 128, False)
+        assert y.shape == (37, 640) and y.dtype == torch.bfloat16
+        z = ops.gemm_w4a16(torch.empty(5, 3072, dtype=torch.bfloat16), w, torch.empty(640, 24, dtype=torch.float16),
+                           128, 0)
+        assert z.shape == (5, 640) and z.dtype == torch.bfloat16

@@ -476,3 +476,91 @@ def test_prep_tile_kernel_matches_previous_kernels(M, K, rot, w_in, perm, sr, sm
         outs.append(np.load(f))
         os.remove(f)
     assert np.array_equal(outs[0], outs[1])
+
+
+# ───────────────────────── bf16 W4A16 and low-rank ──────────────────────────
+
+def _bf16_t(a, dev):
+    """float32 numpy holding bf16 values -> bf16 CUDA tensor (exact)."""
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(torch.bfloat16).to(dev)
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+@pytest.mark.parametrize("G", [1, 24])
+@pytest.mark.parametrize("M", [1, 16, 100, 129, 256])
+def test_w4a16_bf16_parity(M, G, layout):
+    """bf16 activations: W = bf16(q * s) from the fp32 product (the reference's
+    PyTorch path, quant_layout.py:81-87 then .to(x.dtype)), bf16 GEMM with
+    fp32 accumulation, bf16 output.  Bar: max-rel 4e-3, the size of one bf16
+    rounding of the output (2^-9 relative) with margin; the W4A16 contract's
+    1e-3 is below bf16's own output resolution."""
+    dev = _dev()
+    N, K = 1024, 3072
+    rng = np.random.default_rng(M * 5 + G)
+    x = O.bf16(rng.standard_normal((M, K)))
+    q = rng.integers(-8, 8, (N, K)).astype(np.int8)
+    packed = _t(O.pack_int4(q), dev)
+    scale = rng.uniform(1e-3, 2e-2, (N, G)).astype(np.float16)
+    w = packed if layout == 0 else rt.repack_int4(packed, K, 1)
+    out = rt.gemm_w4a16(_bf16_t(x, dev), w, _t(scale, dev), group_size=K // G, w_layout=layout)
+    assert out.dtype == torch.bfloat16
+    wb = O.bf16(q.astype(np.float64) * np.repeat(scale.astype(np.float64), K // G, axis=1))
+    ref = x.astype(np.float64) @ wb.astype(np.float64).T
+    assert O.max_rel(out.float().cpu().numpy(), ref) <= 4e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("R", [16, 64, 128, 256])
+def test_lowrank_kernels_any_rank_and_dtype(dtype, R):
+    """mid = T(x @ down^T), out = T(out + s * mid @ up^T) for ranks up to 256
+    in fp16 and bf16 (the reference's F.linear + addmm_, _ops.py:242-243)."""
+    dev = _dev()
+    M, K, N = 40, 1536, 700
+    g = torch.Generator().manual_seed(R)
+    x = torch.randn(M, K, generator=g).to(dtype)
+    down = (torch.randn(R, K, generator=g) * 0.02).to(dtype)
+    up = (torch.randn(N, R, generator=g) * 0.02).to(dtype)
+    base = torch.randn(M, N, generator=g).to(dtype)
+    mid = rt.lowrank_down(x.to(dev), down.to(dev))
+    ref_mid = (x.double() @ down.double().T)
+    assert mid.dtype == dtype
+    tol = 2e-3 if dtype == torch.float16 else 8e-3
+    assert float((mid.cpu().double() - ref_mid).abs().max() / ref_mid.abs().max()) <= tol
+    out = base.to(dev).clone()
+    rt.lowrank_add(out, mid, up.to(dev), 0.7)
+    ref = base.double() + 0.7 * (mid.cpu().double() @ up.double().T)
+    assert float((out.cpu().double() - ref).abs().max() / ref.abs().max()) <= tol
+
+
+def test_w4a16_bf16_with_rank128_lora():
+    dev = _dev()
+    M, N, K, R = 16, 1024, 3072, 128
+    rng = np.random.default_rng(3)
+    x = O.bf16(rng.standard_normal((M, K)))
+    q = rng.integers(-8, 8, (N, K)).astype(np.int8)
+    scale = rng.uniform(1e-3, 2e-2, (N, 24)).astype(np.float16)
+    A = O.bf16(rng.standard_normal((R, K)) * 0.01)
+    B = O.bf16(rng.standard_normal((N, R)) * 0.01)
+    mid = rt.lowrank_down(_bf16_t(x, dev), _bf16_t(A, dev))
+    out = rt.gemm_w4a16(_bf16_t(x, dev), _t(O.pack_int4(q), dev), _t(scale, dev), group_size=128,
+                        lr_mid=mid, lr_up=_bf16_t(B, dev), lr_scale=1.0)
+    wb = O.bf16(q.astype(np.float64) * np.repeat(scale.astype(np.float64), 128, axis=1))
+    ref = x.astype(np.float64) @ wb.T.astype(np.float64) + (x.astype(np.float64) @ A.T.astype(np.float64)) @ B.T
+    assert O.max_rel(out.float().cpu().numpy(), ref) <= 4e-3
+
+
+def test_bounded_wait_runs_out_and_reports_timeout():
+    """A device-side wait that nothing completes gives up after its limit
+    (1 ms here), records IC_DEV_ERR_TIMEOUT for the host and returns; the
+    context stays usable for the next launch."""
+    _dev()
+    L = load("_lib")
+    assert rt.device_error(clear=True) == 0
+    st = __import__("ctypes").c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert L.lib().ic_selftest_wait_timeout(1_000_000, st) == L.IC_OK
+    torch.cuda.synchronize()
+    assert rt.device_error(clear=True) == L.IC_DEV_ERR_TIMEOUT
+    assert rt.device_error(clear=True) == 0            # cleared
+    x = torch.randn(8, 256, device="cuda").half()      # the context still works
+    q, s = rt.dynamic_quantize_activation(x)
+    assert q.shape == (8, 256) and torch.isfinite(s).all()

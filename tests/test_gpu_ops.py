@@ -228,3 +228,55 @@ def test_flux_block_fused_norm_matches_torch_norm():
         assert torch.isfinite(a).all()
         err = (a.float() - b.float()).abs().max() / b.float().abs().max()
         assert err <= 2e-2, float(err)
+
+
+@pytest.mark.parametrize("path", ["pytorch", "w4a16"])
+def test_int4_bf16_activation_paths_with_rank128_lora(path):
+    """bf16 models on the dequant-then-linear INT4 paths, with a rank-128
+    standard LoRA: the reference's PyTorch path (_ops.py:483-491) casts the
+    dequantised weight to the activation dtype, and its LoRA takes any dtype
+    and rank (_ops.py:236-244).  Checked against that math in float64 on the
+    same bf16 values.  Bar: max-rel 4e-3 (bf16 output rounding is 2^-9)."""
+    _dev()
+    kw = {"use_pytorch": True} if path == "pytorch" else {"use_w4a16": True}
+    lin = make_layer("int4_crush", 256, int4_sd(), 512, 128, name="blocks.0.mlp.fc1", **kw)
+    x = h("int4_x").to(torch.bfloat16)
+    g = torch.Generator().manual_seed(7)
+    up = (torch.randn(128, 128, generator=g) * 0.05).to(torch.bfloat16)
+    down = (torch.randn(128, 512, generator=g) * 0.05).to(torch.bfloat16)
+    lin._intcrush_adapter = _Lora(up, down, 64.0)
+    lin._intcrush_lora_strength = 0.5
+    y = lin(x.cuda())
+    assert y.dtype == torch.bfloat16
+    xp = O.prep_activation(x.float().numpy(), smoothrot=h("int4_sr").float().numpy(), rot_need=True, rot_size=256,
+                           w_in=512, perm=G["int4_perm"], int8_path=False, act="bf16")
+    q = O.unpack_int4(G["int4_packed"], 512).astype(np.float64)
+    s = h("int4_s").float().numpy().astype(np.float64).reshape(-1, 1)
+    wb = O.bf16(q * s)
+    ref = xp.astype(np.float64) @ wb.T.astype(np.float64)
+    ref += O.lora_residual(x.float().numpy(), down.float().numpy(), up.float().numpy(), 64.0 / 128 * 0.5)
+    assert O.max_rel(y.float().cpu().numpy(), ref) <= 4e-3
+
+
+def test_torch_custom_ops_match_runtime_calls():
+    """``torch.ops.intcrush_b200.*`` run the same kernels as the ctypes
+    runtime calls: identical bits."""
+    _dev()
+    load("_torch_ops")
+    tops = load("_torch_ops")
+    ops = torch.ops.intcrush_b200
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(300, 3072, generator=g).half().cuda()
+    sr = (torch.rand(3072, generator=g) * 3.5 + 0.5).cuda()
+    perm = torch.randperm(3072, generator=g).int().cuda()
+    xq, s_a = ops.prep_quantize(x, sr, perm, None, 256, 3072)
+    xq2, s_a2, _, _ = rt.prep_quantize(x, smoothrot=sr, rot_size=256, w_in=3072, perm=perm)
+    assert torch.equal(xq, xq2) and torch.equal(s_a, s_a2)
+    q = torch.randint(-8, 8, (640, 3072), generator=g, dtype=torch.int8)
+    qu = (q.to(torch.int16) & 0xF).to(torch.uint8)
+    packed = (qu[:, 0::2] | (qu[:, 1::2] << 4)).contiguous().cuda()
+    s_w = (torch.rand(640, 24, generator=g) * 1e-2 + 1e-3).cuda()
+    y = ops.gemm_a8(xq, packed, s_w, s_a, None, tops.dtype_code(torch.float16), 128, False)
+    assert torch.equal(y, rt.gemm_a8(xq2, packed, s_w, s_a2, out_dtype=torch.float16, group_size=128))
+    z = ops.gemm_w4a16(x[:16], packed, s_w.half(), 128, 0)
+    assert torch.equal(z, rt.gemm_w4a16(x[:16], packed, s_w.half(), group_size=128))
