@@ -385,6 +385,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     tot_ms, e2e_ms, gemm_sum, prep_sum = vals.tolist()
     # DiT-block numbers at the same N (every rank takes part)
     block = None if args.no_secondary else flux_block_secondary(args, rank, world, local_rank, dev, rt)
+    feat = None if (args.no_secondary or world == 1) else feature_sharded_secondary(world, rank, dev)
 
     if rank != 0:
         return
@@ -420,6 +421,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> None:
     }
     if block is not None:
         line.setdefault("secondary", {})["flux_block"] = block
+    if feat is not None:
+        line.setdefault("secondary", {})["feature_sharded"] = feat
     if world == 1 and not args.no_secondary:
         line.setdefault("secondary", {}).update(secondary_lines(dev, flush, hbm, int8_peak, bf16))
         line["secondary"]["gpu_comparators"] = gpu_comparators(dev, flush, d, w_rep, perm32)
@@ -640,6 +643,50 @@ def gpu_comparators(dev, flush, d, w_rep, perm32, reps: int = 10) -> dict:
         t_t = timed(lambda: F.linear(x3, dequant_f16()))
         out[f"w4a16_m{M3}"] = {"ours_ms": t_ours, "torch_dequant_linear_ms": t_t, "ratio": t_t / t_ours}
     return out
+
+
+def feature_sharded_secondary(world: int, rank: int, dev, steps: int = 5) -> dict:
+    """The config-2 layer split by output features over the ranks (each rank
+    holds N / world weight rows, preps the same 4096 tokens, runs its GEMM
+    slice; an NCCL all-gather assembles [M, N]; strong scaling).  Timed two
+    ways: one all-gather after the whole GEMM, and the GEMM in 4 token chunks
+    with each chunk's all-gather issued asynchronously behind the next
+    chunk's GEMM.  Max over ranks of the per-call time."""
+    import importlib
+    import torch
+    import torch.distributed as dist
+    sh = importlib.import_module(PKG + "._sharded")
+    d = make_inputs(seed=0, device=dev)
+    lin = sh.FeatureShardedLinear(d["packed"], d["scale"], d["bias"], group_size=GS, smoothrot=d["smoothrot"],
+                                  rot_size=ROT, w_in=K, perm=d["perm"], device=dev)
+    st = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+    with torch.no_grad():
+        plain = lin(d["x"])
+        ov = lin.forward_overlapped(d["x"], chunks=4)
+        same = bool(torch.equal(plain, ov))
+        t_plain = timed(lambda: lin(d["x"]))
+        t_ov = timed(lambda: lin.forward_overlapped(d["x"], chunks=4))
+        t_local = timed(lambda: lin.local_forward(d["x"], torch.float16))
+    return {"tops": OPS / (min(t_plain, t_ov) * 1e-3) / 1e12, "ms_all_gather_after_gemm": t_plain,
+            "ms_chunked_overlap": t_ov, "ms_local_gemm_only": t_local, "n_gpus": world,
+            "all_gather_bytes_per_rank": M * (-(-N // world)) * 2 * (world - 1),
+            "overlapped_equals_plain": same,
+            "layout": f"output-feature-sharded x{world}: N/{world} weight rows per GPU, NCCL all-gather of [M, N]"}
 
 
 def flux_block_secondary(args, rank: int, world: int, local_rank: int, dev, rt, steps: int = 5) -> dict:

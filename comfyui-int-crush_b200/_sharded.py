@@ -123,3 +123,35 @@ class FeatureShardedLinear:
         dist.all_gather(parts, local.contiguous(), group=self.group)
         out = torch.cat(parts, dim=1)[:, :self.N]
         return out.reshape(*lead, self.N)
+
+    def forward_overlapped(self, x: torch.Tensor, chunks: int = 4) -> torch.Tensor:
+        """Same result as ``__call__`` with the all-gather hidden behind the
+        GEMM: the tokens are prepped once, then the GEMM runs chunk by chunk
+        (``chunks`` contiguous token ranges) and each chunk's all-gather is
+        issued asynchronously as soon as its GEMM is queued, so the exchange
+        of chunk i overlaps the GEMM of chunk i + 1 (NCCL runs on its own
+        stream, ordered after the chunk's GEMM).  The chunks are assembled
+        into ``[M, N]`` once every exchange has completed."""
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        if self.world == 1:
+            return self(x)
+        M = x2.shape[0]
+        xq, s_a, _, _ = self._prep(x2, smoothrot=self.smoothrot, rot_size=self.rot_size, w_in=self.w_in,
+                                   perm=self.perm, smooth=self.smooth)
+        kw = {"repacked": True} if self.repacked else {}
+        step = -(-M // max(1, chunks))
+        step = -(-step // 128) * 128 if step > 128 else step   # whole token tiles per chunk
+        pending = []
+        for m0 in range(0, M, step):
+            m1 = min(M, m0 + step)
+            local = self._gemm(xq[m0:m1], self.weight, self.scale, s_a[m0:m1], bias=self.bias,
+                               out_dtype=x.dtype, group_size=self.group_size, **kw).contiguous()
+            parts = [torch.empty_like(local) for _ in range(self.world)]
+            work = dist.all_gather(parts, local, group=self.group, async_op=True)
+            pending.append((m0, m1, parts, work, local))
+        out = torch.empty((M, self.N), dtype=x.dtype, device=x2.device)
+        for m0, m1, parts, work, _ in pending:
+            work.wait()
+            out[m0:m1] = torch.cat(parts, dim=1)[:, :self.N]
+        return out.reshape(*lead, self.N)

@@ -134,22 +134,32 @@ def test_ops_refuse_cpu_tensors():
 
 
 # ── loaders ─────────────────────────────────────────────────────────────────
-def test_detect_rot_size():
-    d = loaders._detect_rot_size
-    assert d(None, 256, ("1",)) == 256
-    assert d({"int_crush.format_version": "1", "int_crush.rot_size": "1024"}, 256, ("1",)) == 1024
-    assert d({"int_crush.format_version": "2", "int_crush.rot_size": "1024"}, 256, ("1",)) == 256
-    assert d({"int_crush.format_version": "1", "int_crush.rot_size": "48"}, 256, ("1",)) == 256
-    assert d({"int_crush.format_version": "3"}, 64, ("2", "3")) == 64
+def test_checkpoint_rot_size_from_metadata():
+    info = loaders.CheckpointInfo
+    assert info({}).rot_size(256, ("1",)) == 256
+    assert info({"int_crush.format_version": "1", "int_crush.rot_size": "1024"}).rot_size(256, ("1",)) == 1024
+    assert info({"int_crush.format_version": "2", "int_crush.rot_size": "1024"}).rot_size(256, ("1",)) == 256
+    assert info({"int_crush.format_version": "1", "int_crush.rot_size": "48"}).rot_size(256, ("1",)) == 256
+    assert info({"int_crush.format_version": "3"}).rot_size(64, ("2", "3")) == 64
 
 
-def test_parse_padded_layers_and_node_api():
-    assert loaders._parse_padded_layers("img_in.weight=64; a.b.weight=3072") == {"img_in.weight": 64,
-                                                                                  "a.b.weight": 3072}
+def test_padded_layers_and_node_api():
+    meta = {"int_crush.padded_layers": "img_in.weight=64; a.b.weight=3072"}
+    assert loaders.CheckpointInfo(meta).padded_layers() == {"img_in.weight": 64, "a.b.weight": 3072}
+    assert loaders.CheckpointInfo({}).padded_layers() == {}
     for cls in ("SimpleINT4UNetLoader", "SimpleINT8UNetLoader", "IntCrushLoRALoader", "IntCrushLoRAUnloader"):
         c = loaders.NODE_CLASS_MAPPINGS[cls]
         assert c.CATEGORY == "loaders/INT-Crush" and "required" in c.INPUT_TYPES()
+        assert c.RETURN_TYPES == ("MODEL",) and callable(getattr(c, c.FUNCTION))
     assert loaders.SimpleINT4UNetLoader.INPUT_TYPES()["required"]["rot_size"][0] == [0, 16, 64, 256, 1024, 4096]
+    assert loaders.SimpleINT4UNetLoader.INPUT_TYPES()["required"]["rot_size"][1] == {"default": 256}
+
+
+def test_int4_loader_without_rotation_uses_w4a16():
+    ops_cls = loaders.SimpleINT4UNetLoader()._ops_for(0)
+    lin = ops_cls.Linear(64, 32)
+    assert lin._intcrush_use_w4a16 is True
+    assert loaders.SimpleINT4UNetLoader()._ops_for(256).Linear(64, 32)._intcrush_use_w4a16 is False
 
 
 # ── layer loading (no forward on CPU) ───────────────────────────────────────

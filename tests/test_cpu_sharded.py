@@ -72,6 +72,10 @@ def _worker(rank, world, port, N, out_q):
         lin = sh.FeatureShardedLinear(w, s_w, bias, group_size=128, smoothrot=sr, rot_size=64, w_in=256,
                                       perm=perm, prep=_oracle_prep, gemm=_oracle_gemm)
         y = lin(x.to(torch.float32))
+        # the chunked form (async all-gather per token chunk) gives the same bits
+        x_long = torch.cat([x] * 50).to(torch.float32)          # 300 tokens: 3 chunks of 128 / 44
+        y_ov = lin.forward_overlapped(x_long, chunks=3)
+        assert torch.equal(y_ov, lin(x_long)), "overlapped form differs"
         out_q.put((rank, lin.weight.shape[0], y.numpy()))
     finally:
         dist.destroy_process_group()

@@ -280,3 +280,35 @@ def test_torch_custom_ops_match_runtime_calls():
     assert torch.equal(y, rt.gemm_a8(xq2, packed, s_w, s_a2, out_dtype=torch.float16, group_size=128))
     z = ops.gemm_w4a16(x[:16], packed, s_w.half(), 128, 0)
     assert torch.equal(z, rt.gemm_w4a16(x[:16], packed, s_w.half(), group_size=128))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_convlinear_modules_on_cuda(dtype):
+    """ConvLinear4bit (B200 prep + W4A16 kernels) and ConvLinear8bit (B200
+    prep, torch dequantised linear) against their math in float64: rotate,
+    permute, dequantise per row, linear, bias."""
+    _dev()
+    conv = load("convlinear")
+    qu = load("_quant_utils")
+    g = torch.Generator().manual_seed(4)
+    lin = torch.nn.Linear(512, 192)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(192, 512, generator=g) * 0.05)
+        lin.bias.copy_(torch.randn(192, generator=g) * 0.02)
+    perm = torch.randperm(512, generator=g)
+    x = torch.randn(40, 512, generator=g).to(dtype)
+    m4 = conv.ConvLinear4bit.from_float(lin, rot_need=True, rot_size=64, perm=perm).cuda()
+    m8 = conv.ConvLinear8bit.from_float(lin, rot_need=True, rot_size=64).cuda()
+    y4 = m4(x.cuda())
+    y8 = m8(x.cuda())
+    assert y4.dtype == dtype and y8.dtype == dtype
+    H = torch.from_numpy(O.hadamard(64))
+    xr = (x.double().reshape(40, 8, 64) @ H.T).reshape(40, 512).to(dtype).double()
+    w4 = qu.unpack_int4(m4.weight.cpu(), 512).double() * m4.scale.cpu().double().reshape(-1, 1)
+    w4 = w4.to(dtype).double()
+    ref4 = xr[:, perm] @ w4.T + lin.bias.detach().double()
+    w8 = (m8.weight.cpu().to(dtype) * m8.scale.cpu().to(dtype)).double()
+    ref8 = xr @ w8.T + lin.bias.detach().double()
+    tol = 1e-3 if dtype == torch.float16 else 4e-3
+    assert float((y4.cpu().double() - ref4).abs().max() / ref4.abs().max()) <= tol
+    assert float((y8.cpu().double() - ref8).abs().max() / ref8.abs().max()) <= tol
