@@ -770,11 +770,12 @@ class _QLinear:
         self.b = (torch.randn(n_out, generator=g) * 0.02).half().to(dev)
         self.n_in = n_in
 
-    def __call__(self, x, norm=None):
+    def __call__(self, x, norm=None, activation=0):
         x2 = x.reshape(-1, x.shape[-1])
         xq, s_a, _, _ = self.rt.prep_quantize(x2, smoothrot=self.sr, rot_size=ROT, w_in=self.n_in, perm=self.perm,
                                               norm=norm)
-        y = self.rt.gemm_a8(xq, self.w, self.s, s_a, bias=self.b, out_dtype=x.dtype, group_size=GS, repacked=True)
+        y = self.rt.gemm_a8(xq, self.w, self.s, s_a, bias=self.b, out_dtype=x.dtype, group_size=GS, repacked=True,
+                            activation=activation)
         return y.reshape(*x.shape[:-1], y.shape[-1])
 
 
@@ -825,6 +826,8 @@ class FluxDoubleBlock:
         self.qn = {s: (1 + 0.1 * torch.randn(128, generator=g)).to(dtype).to(dev) for s in ("img", "txt")}
         self.kn = {s: (1 + 0.1 * torch.randn(128, generator=g)).to(dtype).to(dev) for s in ("img", "txt")}
         self.mlp = mlp
+        # the quantised layer applies GELU(tanh) in the fc1 GEMM epilogue
+        self.fused_gelu = linear is None
 
     def linear_ops(self, n_img: int, n_txt: int) -> float:
         h, m = self.h, self.mlp
@@ -858,11 +861,14 @@ class FluxDoubleBlock:
         for s, x, att in (("txt", txt, a[:, :nt]), ("img", img, a[:, nt:])):
             _, _, g1, sh2, sc2, g2 = mods[s]
             x = x + g1[:, None] * self.proj[s](att)
+            kw = {"activation": 3} if self.fused_gelu else {}
             if self.fused_norm:
-                f1 = self.fc1[s](x, norm=("layer", (1 + sc2[0]).float(), sh2[0].float(), 1e-6))
+                f1 = self.fc1[s](x, norm=("layer", (1 + sc2[0]).float(), sh2[0].float(), 1e-6), **kw)
             else:
-                f1 = self.fc1[s](F.layer_norm(x, (h,), eps=1e-6) * (1 + sc2[:, None]) + sh2[:, None])
-            x = x + g2[:, None] * self.fc2[s](F.gelu(f1, approximate="tanh"))
+                f1 = self.fc1[s](F.layer_norm(x, (h,), eps=1e-6) * (1 + sc2[:, None]) + sh2[:, None], **kw)
+            if not self.fused_gelu:
+                f1 = F.gelu(f1, approximate="tanh")
+            x = x + g2[:, None] * self.fc2[s](f1)
             outs.append(x)
         return outs[1], outs[0]
 
@@ -882,10 +888,10 @@ class _QLinear8:
         self.s = (torch.rand(n_out, generator=g) * 1e-4 + 2e-5).float().to(dev)
         self.b = (torch.randn(n_out, generator=g) * 0.02).half().to(dev)
 
-    def __call__(self, x):
+    def __call__(self, x, activation=0):
         x2 = x.reshape(-1, x.shape[-1])
         xq, s_a, _, _ = self.rt.prep_quantize(x2, rot_size=self.rot)
-        y = self.rt.gemm_a8(xq, self.w, self.s, s_a, bias=self.b, out_dtype=x.dtype)
+        y = self.rt.gemm_a8(xq, self.w, self.s, s_a, bias=self.b, out_dtype=x.dtype, activation=activation)
         return y.reshape(*x.shape[:-1], y.shape[-1])
 
 
@@ -937,7 +943,7 @@ class WanBlock:
         a = F.scaled_dot_product_attention(cq, ck, cv).transpose(1, 2).reshape(B, L, h)
         x = x + self.co(a)
         y = F.layer_norm(x, (h,), eps=1e-6) * (1 + sc2) + sh2
-        return x + g2 * self.fc2(F.gelu(self.fc1(y), approximate="tanh"))
+        return x + g2 * self.fc2(self.fc1(y, activation=3))   # GELU(tanh) in the fc1 epilogue
 
 
 def run_wan(args, rank: int, world: int, local_rank: int) -> None:

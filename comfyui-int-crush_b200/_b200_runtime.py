@@ -249,8 +249,14 @@ def gemm_a8(
     zp_corr: torch.Tensor | None = None,
     repacked: bool = False,
     splits: int | None = None,
+    activation: int = 0,
+    residual: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """``out = s_a[m] * sum_g s_w[n,g] * (xq @ w^T)_g + bias - rowsum (x) zp_corr``.
+
+    ``activation`` (0 none, 1 SiLU, 2 GELU erf, 3 GELU tanh) and then
+    ``residual`` ([M, N], any float dtype, unit column stride) are applied in
+    fp32 in the epilogue before the output cast.
 
     ``w`` is int8 ``[N, K]`` or packed INT4 uint8 ``[N, K/2]``; ``s_w`` is
     ``[N]``/``[N,1]`` (per channel) or ``[N, G]`` (groups of ``group_size``,
@@ -299,6 +305,23 @@ def gemm_a8(
     zc = _f32c(zp_corr)
     if splits is None:
         splits = _auto_splits(M, N, K, G, gs, x_int8.device, kind != L.IC_W_INT8)
+    if activation or residual is not None:
+        r = residual
+        if r is not None:
+            if r.shape != (M, N):
+                raise AssertionError(f"residual shape mismatch: {tuple(r.shape)} vs ({M}, {N})")
+            _need_cuda("gemm_a8", r)
+            if r.stride(1) != 1:
+                r = r.contiguous()
+        ws = torch.empty(splits * M * N if splits > 1 else 0, dtype=torch.float32, device=x_int8.device)
+        st = L.lib().ic_gemm_a8_ex(
+            _p(x_int8), M, K, x_int8.stride(0), _p(w), kind, N, w.stride(0), _p(sw), G, gs, _p(sa),
+            _p(b), _DT[b.dtype] if b is not None else 0, _p(rs), _p(zc), int(activation),
+            _p(r), _DT[r.dtype] if r is not None else 0, r.stride(0) if r is not None else 0,
+            _p(out), _DT[out.dtype], out.stride(0), int(splits), _p(ws) if splits > 1 else None, ws.numel(),
+            _stream(x_int8))
+        L.check(st, "ic_gemm_a8_ex")
+        return out
     if splits > 1:
         ws = torch.empty(splits * M * N, dtype=torch.float32, device=x_int8.device)
         st = L.lib().ic_gemm_a8_splitk(
@@ -364,14 +387,82 @@ def fused_int8_gemm_dequant(
     residual: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """``kernels/triton_int8_gemm.py:135-205`` on tcgen05 (kind::i8).
+    """``kernels/triton_int8_gemm.py:135-205`` on tcgen05 (kind::i8), with
+    the reference's epilogue: ``activation`` 0 none, 1 SiLU, 2 GELU (erf),
+    plus 3 GELU with the tanh approximation; then ``+ residual``."""
+    if activation not in (0, 1, 2, 3):
+        raise ValueError(f"activation must be 0, 1, 2 or 3, got {activation}")
+    return gemm_a8(x_int8, w_int8, s_w, s_a, bias=bias, out_dtype=out_dtype, out=out, activation=activation,
+                   residual=residual)
 
-    The SiLU/GELU and residual epilogues of the reference are never used by
-    its forward path (``_ops.py``) and are not built here.
+
+def int8_gemm_int8out(
+    x_int8: torch.Tensor,
+    w_int8: torch.Tensor,
+    s_w: torch.Tensor,
+    s_a: torch.Tensor,
+    c_out: torch.Tensor | None = None,
+    s_c_out: torch.Tensor | None = None,
+    bias: torch.Tensor | None = None,
+    activation: int = 0,
+    group_size: int | None = None,
+    repacked: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """``kernels/triton_int8_gemm.py:472-536``: a GEMM whose output is
+    re-quantised to int8 for the next GEMM of a chain (``s_c`` feeds it as
+    ``s_a``).
+
+    The scale is row-global: ``s_c[m] = max(max_n |y[m, n]|, 1e-8) / 127``
+    over the whole output row, ``c = rint(y / s_c)`` (ties to even), so that
+    ``(c, s_c)`` equals ``dynamic_quantize_activation`` of the fp32 output,
+    which the reference's docstring promises.  (The reference kernel takes
+    the max over one BLOCK_N tile and lets the tiles of a row race on
+    ``s_c``.)  Weights may be int8 or packed INT4 (``group_size`` /
+    ``repacked`` as in :func:`gemm_a8`).
     """
-    if activation != 0 or residual is not None:
-        raise NotImplementedError("activation / residual epilogues are not part of the forward path")
-    return gemm_a8(x_int8, w_int8, s_w, s_a, bias=bias, out_dtype=out_dtype, out=out)
+    _need_cuda("int8_gemm_int8out", x_int8, w_int8, s_w, s_a, c_out, s_c_out, bias)
+    if x_int8.dtype != torch.int8:
+        raise AssertionError(f"x_int8 must be int8, got {x_int8.dtype}")
+    M, K = x_int8.shape
+    if x_int8.stride(1) != 1:
+        x_int8 = x_int8.contiguous()
+    if w_int8.dtype == torch.int8:
+        kind, N = L.IC_W_INT8, w_int8.shape[0]
+        if w_int8.shape[1] != K:
+            raise AssertionError(f"K mismatch: {K} vs {w_int8.shape[1]}")
+    elif w_int8.dtype == torch.uint8:
+        kind, N = (L.IC_W_INT4R if repacked else L.IC_W_INT4), w_int8.shape[0]
+        if w_int8.shape[1] != (K + 1) // 2:
+            raise AssertionError(f"packed K mismatch: {K} vs {w_int8.shape[1]} bytes")
+    else:
+        raise AssertionError(f"w must be int8 or uint8 (packed int4), got {w_int8.dtype}")
+    w = w_int8 if w_int8.stride(1) == 1 else w_int8.contiguous()
+    sw = s_w.to(torch.float32).reshape(N, -1).contiguous()
+    G = sw.shape[1]
+    if G > 1 and group_size is None:
+        group_size = -(-K // G)
+    gs = int(group_size) if G > 1 else K
+    sa = s_a.to(torch.float32).contiguous()
+    if c_out is not None:
+        if c_out.shape != (M, N) or c_out.dtype != torch.int8 or c_out.stride(1) != 1:
+            raise AssertionError(f"c_out must be int8 [{M}, {N}] with unit column stride")
+        c = c_out
+    else:
+        c = torch.empty((M, N), dtype=torch.int8, device=x_int8.device)
+    if s_c_out is not None:
+        if s_c_out.shape != (M,) or s_c_out.dtype != torch.float32 or not s_c_out.is_contiguous():
+            raise AssertionError(f"s_c_out must be contiguous float32 [{M}]")
+        s_c = s_c_out
+    else:
+        s_c = torch.empty(M, dtype=torch.float32, device=x_int8.device)
+    b = None if bias is None else bias.contiguous()
+    ws = torch.empty(M * N + M, dtype=torch.float32, device=x_int8.device)
+    st = L.lib().ic_gemm_a8_int8out(
+        _p(x_int8), M, K, x_int8.stride(0), _p(w), kind, N, w.stride(0), _p(sw), G, gs, _p(sa),
+        _p(b), _DT[b.dtype] if b is not None else 0, int(activation), _p(c), c.stride(0), _p(s_c),
+        _p(ws), ws.numel(), _stream(x_int8))
+    L.check(st, "ic_gemm_a8_int8out")
+    return c, s_c
 
 
 def fused_w4a8_gemm_dequant(
@@ -540,7 +631,7 @@ __all__ = [
     "TRITON_AVAILABLE", "TRITON_INT4_UNPACK", "TRITON_INT8_GEMM", "TRITON_INT4_INT8_UNPACK",
     "TRITON_DYNQUANT", "TRITON_W4A8_GEMM", "TRITON_FUSED_QGD", "USE_FUSED_W8A8", "USE_CUDA_GRAPHS",
     "B200_AVAILABLE", "B200_LIBRARY_LOADED",
-    "dynamic_quantize_activation", "fused_int8_gemm_dequant", "fused_quant_int8_gemm_dequant",
+    "dynamic_quantize_activation", "fused_int8_gemm_dequant", "int8_gemm_int8out", "fused_quant_int8_gemm_dequant",
     "fused_w4a8_gemm_dequant", "unpack_int4_to_int8", "unpack_int4_to_float16",
     "prep_quantize", "gemm_a8", "gemm_w4a16", "repack_int4", "lowrank_down", "lowrank_add", "device_error",
     "fused_layernorm_quantize", "fused_rmsnorm_quantize",

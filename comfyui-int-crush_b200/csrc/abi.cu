@@ -160,12 +160,23 @@ int ic_dynamic_quantize(const void* x, int x_dtype, int64_t M, int64_t K, int64_
                        nullptr, stream);
 }
 
+struct EpiArgs {
+  int act = 0;
+  const void* residual = nullptr;
+  int residual_dtype = 0;
+  int64_t ldr = 0;
+  float* rowmax = nullptr;
+};
+
 static int gemm_a8_impl(const char* fn, const int8_t* xq, int64_t M, int64_t K, int64_t ldq, const void* w, int w_kind, int64_t N,
                int64_t ldw, const float* s_w, int64_t G, int64_t group_size, const float* s_a,
                const void* bias, int bias_dtype, const float* rowsum, const float* zp_corr, void* out,
                int out_dtype, int64_t ldo, int splits, float* ws, int64_t ws_elems,
-                        void* stream) {
+                        void* stream, const EpiArgs& epi = EpiArgs()) {
   g_err[0] = 0;
+  if (epi.act < 0 || epi.act > 3) return fail(IC_ERR_ARG, "%s: activation must be 0 (none), 1 (SiLU), 2 (GELU) or 3 (GELU tanh)", fn);
+  if (epi.residual && (epi.residual_dtype < IC_DTYPE_F16 || epi.residual_dtype > IC_DTYPE_F32 || epi.ldr < N))
+    return fail(IC_ERR_ARG, "%s: residual needs a dtype code and ldr >= N", fn);
   if (M < 0 || N < 0 || K <= 0) return fail(IC_ERR_ARG, "%s: bad M/N/K", fn);
   if (M == 0 || N == 0) return IC_OK;
   if (!xq || !w || !s_w || !s_a || !out) return fail(IC_ERR_ARG, "%s: NULL operand", fn);
@@ -212,6 +223,8 @@ static int gemm_a8_impl(const char* fn, const int8_t* xq, int64_t M, int64_t K, 
   }
   a.splits = splits;
   a.ws = ws;
+  a.act = epi.act; a.residual = epi.residual; a.residual_dtype = epi.residual_dtype; a.ldr = epi.ldr;
+  a.rowmax = epi.rowmax;
   const char* why = "kernel launch";
   const int force_bn = 0;
   cudaError_t e = ic::launch_gemm_a8(xq, (int)M, (int)K, ldq, w, w_kind == IC_W_INT8 ? IC_W_INT8 : IC_W_INT4, (int)N, ldw, a, force_bn,
@@ -234,6 +247,43 @@ int ic_gemm_a8_splitk(const int8_t* xq, int64_t M, int64_t K, int64_t ldq, const
                       void* stream) {
   return gemm_a8_impl("ic_gemm_a8_splitk", xq, M, K, ldq, w, w_kind, N, ldw, s_w, G, group_size, s_a, bias,
                       bias_dtype, rowsum, zp_corr, out, out_dtype, ldo, splits, workspace, workspace_elems, stream);
+}
+
+int ic_gemm_a8_ex(const int8_t* xq, int64_t M, int64_t K, int64_t ldq, const void* w, int w_kind, int64_t N,
+                  int64_t ldw, const float* s_w, int64_t G, int64_t group_size, const float* s_a,
+                  const void* bias, int bias_dtype, const float* rowsum, const float* zp_corr, int activation,
+                  const void* residual, int residual_dtype, int64_t ldr, void* out, int out_dtype, int64_t ldo,
+                  int splits, float* workspace, int64_t workspace_elems, void* stream) {
+  EpiArgs e;
+  e.act = activation; e.residual = residual; e.residual_dtype = residual_dtype; e.ldr = ldr;
+  return gemm_a8_impl("ic_gemm_a8_ex", xq, M, K, ldq, w, w_kind, N, ldw, s_w, G, group_size, s_a, bias,
+                      bias_dtype, rowsum, zp_corr, out, out_dtype, ldo, splits, workspace, workspace_elems, stream, e);
+}
+
+int ic_gemm_a8_int8out(const int8_t* xq, int64_t M, int64_t K, int64_t ldq, const void* w, int w_kind, int64_t N,
+                       int64_t ldw, const float* s_w, int64_t G, int64_t group_size, const float* s_a,
+                       const void* bias, int bias_dtype, int activation, int8_t* c, int64_t ldc, float* s_c,
+                       float* workspace, int64_t workspace_elems, void* stream) {
+  const char* fn = "ic_gemm_a8_int8out";
+  g_err[0] = 0;
+  if (M < 0 || N < 0) return fail(IC_ERR_ARG, "%s: bad M/N", fn);
+  if (M == 0 || N == 0) return IC_OK;
+  if (!c || !s_c || !workspace) return fail(IC_ERR_ARG, "%s: NULL output or workspace", fn);
+  if (ldc < N) return fail(IC_ERR_ARG, "%s: ldc < N", fn);
+  if (M > 0x7fffffffLL || N > 0x7fffffffLL) return fail(IC_ERR_UNSUPPORTED, "%s: dims >= 2^31", fn);
+  // workspace: the fp32 epilogue values [M, N], then the row maxima [M]
+  if ((__int128)workspace_elems < (__int128)M * N + M) return fail(IC_ERR_ARG, "%s: workspace needs M*N + M floats", fn);
+  float* y = workspace;
+  float* rowmax = workspace + M * N;
+  cudaError_t er = cudaMemsetAsync(rowmax, 0, (size_t)M * sizeof(float), (cudaStream_t)stream);
+  if (er != cudaSuccess) return cuda_status(er, "clearing the row maxima");
+  EpiArgs e;
+  e.act = activation; e.rowmax = rowmax;
+  const int st = gemm_a8_impl(fn, xq, M, K, ldq, w, w_kind, N, ldw, s_w, G, group_size, s_a, bias, bias_dtype,
+                              nullptr, nullptr, y, IC_DTYPE_F32, N, 1, nullptr, 0, stream, e);
+  if (st != IC_OK) return st;
+  return cuda_status(ic::launch_requant_rows(y, (int)M, (int)N, N, rowmax, c, ldc, s_c, (cudaStream_t)stream),
+                     "ic_gemm_a8_int8out requantisation launch");
 }
 
 // ---------------------------------------------------------------------------

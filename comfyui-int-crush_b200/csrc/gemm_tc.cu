@@ -73,7 +73,27 @@ struct GemmArgs {
   int kb_per_unit;
   float* ws;
   int group_m;      // tile order: all weight tiles of group_m consecutive token tiles, then the next group
+  // optional epilogue after dequantisation + bias: act (0 none, 1 SiLU,
+  // 2 GELU (erf), 3 GELU (tanh)), then + residual[m, n] (row stride ldr),
+  // then (INT8-out) the row's running |max| into rowmax[m]
+  int act;
+  const void* residual;
+  int residual_dtype;
+  long long ldr;
+  float* rowmax;
 };
+
+// The activation epilogue of fused_int8_gemm_dequant
+// (kernels/triton_int8_gemm.py:119-123): SiLU x * sigmoid(x), GELU
+// 0.5 x (1 + erf(x / sqrt 2)); 3 adds the tanh form of GELU that Flux-class
+// MLPs use (0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3)))).
+__device__ __forceinline__ float apply_act(int act, float y) {
+  if (act == 1) return y / (1.f + expf(-y));
+  if (act == 2) return 0.5f * y * (1.f + erff(y * 0.70710678118654752f));
+  if (act == 3) return 0.5f * y * (1.f + tanhf(0.79788456080286536f * fmaf(0.044715f * y, y * y, y)));
+  return y;
+}
+__device__ __forceinline__ bool epi_extra(const GemmArgs& a) { return a.act || a.residual || a.rowmax; }
 
 // Tile index -> (weight tile, token tile).  Tiles run in groups of group_m
 // token tiles; within a group the token tile varies fastest.  A wave of CTAs
@@ -216,11 +236,21 @@ __device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const f
   const int jmax = nvalid ? min(width, a.M - m0) : 0;   // valid tokens in this chunk
   T* p = out + (size_t)m0 * a.ldo + n;
   float sa_b = sa_l, rs_b = rs_l;
+  const bool extra = epi_extra(a);
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const float sa = __shfl_sync(0xffffffffu, sa_b, j);
     const float rs = __shfl_sync(0xffffffffu, rs_b, j);
-    const float y = fmaf(-rs, zpc_n, fmaf(v[j], sa, bias_n));
+    float y = fmaf(-rs, zpc_n, fmaf(v[j], sa, bias_n));
+    if (extra) {
+      y = apply_act(a.act, y);
+      if (a.residual && j < jmax) y += load_any(a.residual, a.residual_dtype, (size_t)(m0 + j) * a.ldr + n);
+      if (a.rowmax) {   // one atomic per token per warp: the max over the warp's 32 features first
+        float am = (j < jmax) ? fabsf(y) : 0.f;
+        asm("redux.sync.max.f32 %0, %0, 0xffffffff;" : "+f"(am));
+        if (lane == 0 && m0 + j < a.M) atomicMax(reinterpret_cast<int*>(a.rowmax) + m0 + j, __float_as_int(am));
+      }
+    }
     if (j < jmax) {
       if constexpr (sizeof(T) == 4) *p = y;
       else if constexpr (std::is_same<T, __half>::value) *p = __float2half_rn(y);
@@ -259,7 +289,7 @@ __device__ __forceinline__ void store_partial(const GemmArgs& a, const float* v,
   }
 }
 
-// out[m, n] = sum_s ws[s, m, n] + bias[n] - rowsum[m] * zp_corr[n]
+// out[m, n] = epilogue(sum_s ws[s, m, n] + bias[n] - rowsum[m] * zp_corr[n])
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmArgs a) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long MN = (long long)a.M * a.N;
@@ -270,7 +300,36 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmArgs a) {
   const float bias_n = a.bias ? load_any(a.bias, a.bias_dtype, n) : 0.f;
   const float rs = a.rowsum ? a.rowsum[m] : 0.f;
   const float zc = a.zp_corr ? a.zp_corr[n] : 0.f;
-  store_out(a.out, a.out_dtype, (size_t)m * a.ldo + n, fmaf(-rs, zc, v + bias_n));
+  float y = fmaf(-rs, zc, v + bias_n);
+  if (epi_extra(a)) {
+    y = apply_act(a.act, y);
+    if (a.residual) y += load_any(a.residual, a.residual_dtype, (size_t)m * a.ldr + n);
+    if (a.rowmax) atomicMax(reinterpret_cast<int*>(a.rowmax) + m, __float_as_int(fabsf(y)));
+  }
+  store_out(a.out, a.out_dtype, (size_t)m * a.ldo + n, y);
+}
+
+// INT8 output with a row-global scale: s_c[m] = max(rowmax[m], 1e-8) / 127,
+// q = rint(y / s_c) ties to even (the quantiser of
+// kernels/triton_quantize.py:43-54), from the fp32 epilogue values y.
+__global__ void __launch_bounds__(256) requant_rows_kernel(const float* y, int M, int N, long long ldy,
+                                                           const float* rowmax, int8_t* q, long long ldq,
+                                                           float* s_c) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)M * N) return;
+  const int m = (int)(i / N), n = (int)(i % N);
+  const float s = __fdiv_rn(fmaxf(rowmax[m], 1e-8f), 127.0f);
+  if (n == 0) s_c[m] = s;
+  const float t = __fdiv_rn(y[(long long)m * ldy + n], s);
+  q[(long long)m * ldq + n] = (int8_t)max(-128, min(127, __float_as_int(t + 12582912.0f) - 0x4B400000));
+}
+
+cudaError_t launch_requant_rows(const float* y, int M, int N, long long ldy, const float* rowmax, int8_t* q,
+                                long long ldq, float* s_c, cudaStream_t st) {
+  const long long mn = (long long)M * N;
+  if (mn == 0) return cudaSuccess;
+  requant_rows_kernel<<<(unsigned)((mn + 255) / 256), 256, 0, st>>>(y, M, N, ldy, rowmax, q, ldq, s_c);
+  return cudaGetLastError();
 }
 
 // W4A16: out[m, n] = fp16(v[j] + bias_n) (no activation scale).

@@ -147,6 +147,35 @@ int ic_gemm_a8_splitk(const int8_t* xq, int64_t M, int64_t K, int64_t ldq,
                       void* out, int out_dtype, int64_t ldo, int splits,
                       float* workspace, int64_t workspace_elems, void* stream);
 
+/* ic_gemm_a8_splitk with the optional epilogue of fused_int8_gemm_dequant
+ * (kernels/triton_int8_gemm.py:119-129, :135-205): after dequantisation,
+ * bias and zero-point term,
+ *   activation 0 none, 1 SiLU x*sigmoid(x), 2 GELU 0.5x(1+erf(x/sqrt 2)),
+ *              3 GELU with the tanh approximation (Flux-class MLPs),
+ * then + residual[m, n] (residual_dtype f16/bf16/f32, row stride ldr; NULL
+ * for none).  splits 1 needs no workspace. */
+int ic_gemm_a8_ex(const int8_t* xq, int64_t M, int64_t K, int64_t ldq,
+                  const void* w, int w_kind, int64_t N, int64_t ldw,
+                  const float* s_w, int64_t G, int64_t group_size, const float* s_a,
+                  const void* bias, int bias_dtype, const float* rowsum, const float* zp_corr,
+                  int activation, const void* residual, int residual_dtype, int64_t ldr,
+                  void* out, int out_dtype, int64_t ldo, int splits,
+                  float* workspace, int64_t workspace_elems, void* stream);
+
+/* INT8-out GEMM for chained layers (int8_gemm_int8out,
+ * kernels/triton_int8_gemm.py:402-536), with a row-global scale instead of
+ * the reference's per-tile one: y = act(dequant GEMM + bias) in fp32,
+ * s_c[m] = max(max_n |y[m, n]|, 1e-8) / 127, c = rint(y / s_c) (ties to even,
+ * clamped), so that (c, s_c) is exactly what dynamic quantisation of the fp32
+ * output would give.  workspace: M*N + M floats (the fp32 values and the row
+ * maxima).  c [M, ldc] int8, s_c [M] fp32. */
+int ic_gemm_a8_int8out(const int8_t* xq, int64_t M, int64_t K, int64_t ldq,
+                       const void* w, int w_kind, int64_t N, int64_t ldw,
+                       const float* s_w, int64_t G, int64_t group_size, const float* s_a,
+                       const void* bias, int bias_dtype, int activation,
+                       int8_t* c, int64_t ldc, float* s_c,
+                       float* workspace, int64_t workspace_elems, void* stream);
+
 /* ic_gemm_a8_splitk with no allocation and no caller workspace.  No
  * counterpart in the reference: it exists for callers that cannot allocate
  * device memory when they run the GEMM -- a C or FFI host without a device

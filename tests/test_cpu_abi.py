@@ -90,3 +90,31 @@ def test_zero_sized_calls_are_no_ops():
     lib = L.lib()
     assert lib.ic_prep_quant(None, 0, 0, 64, 64, None, 0, 64, None, None, None, 0, None, None, None, None) == L.IC_OK
     assert lib.ic_unpack_int4_to_int8(None, 0, 64, 32, None, None) == L.IC_OK
+
+
+def _gemm_ex_args(act=0, residual=None, residual_dtype=0, ldr=0):
+    f = ctypes.c_void_p(256)
+    return [f, 64, 256, 256, f, L.IC_W_INT8, 128, 256, f, 1, 256, f, None, 0, None, None, act, residual,
+            residual_dtype, ldr, f, L.IC_DTYPE_F16, 128, 1, None, 0, None]
+
+
+def test_gemm_epilogue_arguments_validated():
+    lib = L.lib()
+    assert lib.ic_gemm_a8_ex(*_gemm_ex_args(act=4)) == L.IC_ERR_ARG
+    assert b"activation" in lib.ic_last_error()
+    f = ctypes.c_void_p(256)
+    assert lib.ic_gemm_a8_ex(*_gemm_ex_args(residual=f, residual_dtype=L.IC_DTYPE_F16, ldr=64)) == L.IC_ERR_ARG
+    assert lib.ic_gemm_a8_ex(*_gemm_ex_args(residual=f, residual_dtype=9, ldr=128)) == L.IC_ERR_ARG
+
+
+def test_int8out_workspace_and_output_checks():
+    lib = L.lib()
+    f = ctypes.c_void_p(256)
+    base = [f, 64, 256, 256, f, L.IC_W_INT8, 128, 256, f, 1, 256, f, None, 0, 0]
+    # workspace must hold M*N values plus M row maxima
+    assert lib.ic_gemm_a8_int8out(*base, f, 128, f, f, 64 * 128, None) == L.IC_ERR_ARG
+    assert b"M*N + M" in lib.ic_last_error()
+    assert lib.ic_gemm_a8_int8out(*base, f, 64, f, f, 64 * 129, None) == L.IC_ERR_ARG   # ldc < N
+    assert lib.ic_gemm_a8_int8out(*base, None, 128, f, f, 64 * 129, None) == L.IC_ERR_ARG
+    zero = [f, 0] + base[2:]
+    assert lib.ic_gemm_a8_int8out(*zero, f, 128, f, f, 0, None) == L.IC_OK
