@@ -42,7 +42,7 @@ def _hadamard(n: int, dtype: torch.dtype) -> torch.Tensor:
     return H * (1.0 / math.sqrt(n))
 
 
-def prep(x, smoothrot=None, rot_size=0, w_in=None, perm=None, H=None):
+def prep(x, smoothrot=None, rot_size=0, w_in=None, perm=None, H=None, smooth=None):
     x2 = x.reshape(-1, x.shape[-1])
     if smoothrot is not None:
         x2 = x2 / smoothrot.to(x2.dtype)
@@ -57,6 +57,8 @@ def prep(x, smoothrot=None, rot_size=0, w_in=None, perm=None, H=None):
         x2 = F.pad(x2, (0, w_in - x2.shape[-1]))
     if perm is not None:
         x2 = x2[..., perm]
+    if smooth is not None and smoothrot is None:   # INT8 SmoothQuant divide (_ops.py:529-533)
+        x2 = x2 / smooth.to(x2.dtype)
     return x2
 
 
