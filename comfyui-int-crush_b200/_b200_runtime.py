@@ -420,7 +420,7 @@ def int8_gemm_int8out(
     ``s_c``.)  Weights may be int8 or packed INT4 (``group_size`` /
     ``repacked`` as in :func:`gemm_a8`).
     """
-    _need_cuda("int8_gemm_int8out", x_int8, w_int8, s_w, s_a, c_out, s_c_out, bias)
+    _need_cuda("int8_gemm_int8out", "quantize_weight", "lokr_add", x_int8, w_int8, s_w, s_a, c_out, s_c_out, bias)
     if x_int8.dtype != torch.int8:
         raise AssertionError(f"x_int8 must be int8, got {x_int8.dtype}")
     M, K = x_int8.shape
@@ -580,6 +580,56 @@ def lowrank_add(out: torch.Tensor, mid: torch.Tensor, up: torch.Tensor, scale: f
     return out
 
 
+def quantize_weight(w: torch.Tensor, bits: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row requantisation of a float weight on the device (the layout
+    classes' ``quantize``, ``quant_layout.py:100-129,179-200``): returns
+    (packed uint8 ``[N, ceil(K/2)]``, fp16 scales ``[N]``) for ``bits`` 4 and
+    (int8 ``[N, K]``, fp32 scales ``[N]``) for 8."""
+    _need_cuda("quantize_weight", w)
+    if w.dim() != 2:
+        raise AssertionError(f"weight must be 2-D, got {tuple(w.shape)}")
+    wf = w.to(torch.float32)
+    if wf.stride(1) != 1:
+        wf = wf.contiguous()
+    N, K = wf.shape
+    if bits == 4:
+        q = torch.empty((N, (K + 1) // 2), dtype=torch.uint8, device=w.device)
+        s = torch.empty(N, dtype=torch.float16, device=w.device)
+    elif bits == 8:
+        q = torch.empty((N, K), dtype=torch.int8, device=w.device)
+        s = torch.empty(N, dtype=torch.float32, device=w.device)
+    else:
+        raise ValueError(f"bits must be 4 or 8, got {bits}")
+    st = L.lib().ic_quantize_weight(_p(wf), N, K, wf.stride(0), int(bits), _p(q), q.stride(0), _p(s), _stream(wf))
+    L.check(st, "ic_quantize_weight")
+    return q, s
+
+
+def lokr_add(out: torch.Tensor, x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, scale: float) -> torch.Tensor:
+    """``out[t] (viewed [out_l, out_k]) += scale * (w1 @ x[t].view(in_m, in_n)) @ w2^T``
+    in place (``_apply_lokr``, ``_ops.py:88-138``): ``w1`` [out_l, in_m],
+    ``w2`` [out_k, in_n] (the reference's ``w2_t`` transposed), ``out``
+    contiguous [M, out_l * out_k], ``x`` [M, in_m * in_n], all fp16 or bf16.
+    The first product is rounded to the activation dtype, as the
+    reference's matmul does."""
+    _need_cuda("lokr_add", out, x, w1, w2)
+    if out.dtype not in (torch.float16, torch.bfloat16) or {x.dtype, w1.dtype, w2.dtype} != {out.dtype}:
+        raise TypeError("lokr_add: out, x, w1 and w2 must share one dtype, float16 or bfloat16")
+    if not out.is_contiguous():
+        raise AssertionError("lokr_add: out must be contiguous")
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    w1c, w2c = w1.contiguous(), w2.contiguous()
+    M, N = out.shape
+    out_l, in_m = w1c.shape
+    out_k, in_n = w2c.shape
+    temp = torch.empty(M * out_l * in_n, dtype=out.dtype, device=out.device)
+    st = L.lib().ic_lokr_add(_p(out), _DT[out.dtype], M, N, _p(x), x.stride(0), x.shape[1], _p(w1c), out_l, in_m,
+                             _p(w2c), out_k, in_n, float(scale), _p(temp), temp.numel(), _stream(out))
+    L.check(st, "ic_lokr_add")
+    return out
+
+
 def repack_int4(packed: torch.Tensor, K: int, layout: int) -> torch.Tensor:
     """Load-time nibble permutation of packed INT4 weights (``ic_repack_int4``):
     layout 0 feeds ``gemm_a8(..., repacked=True)``, layout 1 feeds
@@ -631,7 +681,7 @@ __all__ = [
     "TRITON_AVAILABLE", "TRITON_INT4_UNPACK", "TRITON_INT8_GEMM", "TRITON_INT4_INT8_UNPACK",
     "TRITON_DYNQUANT", "TRITON_W4A8_GEMM", "TRITON_FUSED_QGD", "USE_FUSED_W8A8", "USE_CUDA_GRAPHS",
     "B200_AVAILABLE", "B200_LIBRARY_LOADED",
-    "dynamic_quantize_activation", "fused_int8_gemm_dequant", "int8_gemm_int8out", "fused_quant_int8_gemm_dequant",
+    "dynamic_quantize_activation", "fused_int8_gemm_dequant", "int8_gemm_int8out", "quantize_weight", "lokr_add", "fused_quant_int8_gemm_dequant",
     "fused_w4a8_gemm_dequant", "unpack_int4_to_int8", "unpack_int4_to_float16",
     "prep_quantize", "gemm_a8", "gemm_w4a16", "repack_int4", "lowrank_down", "lowrank_add", "device_error",
     "fused_layernorm_quantize", "fused_rmsnorm_quantize",

@@ -91,6 +91,12 @@ def _apply_lokr(cache: dict[str, Any], x_raw: torch.Tensor, out: torch.Tensor) -
     T = x_raw.shape[0]
     out_l, in_m = w1.shape
     in_n, out_k = w2_t.shape
+    if (out.is_cuda and out.dtype in (torch.float16, torch.bfloat16) and out.is_contiguous()
+            and x_raw.dtype == out.dtype and in_n <= 256 and out_l * in_m <= 12288):
+        # two B200 kernels: T(w1 @ X_t) per token, then the in-place rank-in_n update
+        if "w2" not in cache:
+            cache["w2"] = w2_t.t().contiguous()
+        return _rt.lokr_add(out, x_raw.reshape(T, -1), w1, cache["w2"], scale)
     chunk = max(1, min(T, (64 << 20) // max(out_l * (in_n + out_k) * x_raw.element_size(), 1)))
     if not out.is_contiguous():
         out = out.contiguous()

@@ -14,7 +14,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libintcrush_b200.so")
-SOURCES = ["intcrush_b200.cu", "ic_common.cuh", "prep_common.cuh", "prep.cu", "prep_tile.cu", "gemm_tc.cu", "skinny.cu", "abi.cu"]
+SOURCES = ["intcrush_b200.cu", "ic_common.cuh", "prep_common.cuh", "prep.cu", "prep_tile.cu", "gemm_tc.cu", "skinny.cu", "weights.cu", "abi.cu"]
 
 
 def _nvcc() -> str:

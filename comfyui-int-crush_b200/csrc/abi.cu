@@ -451,6 +451,44 @@ int ic_lowrank_add(void* out, int64_t M, int64_t N, int64_t ldo, const void* mid
   return ic_lowrank_add_ex(out, IC_DTYPE_F16, M, N, ldo, mid, up, R, scale, stream);
 }
 
+int ic_quantize_weight(const float* w, int64_t N, int64_t K, int64_t ldw, int bits, void* q, int64_t ldq,
+                       void* scale, void* stream) {
+  g_err[0] = 0;
+  if (bits != 4 && bits != 8) return fail(IC_ERR_ARG, "ic_quantize_weight: bits must be 4 or 8");
+  if (N < 0 || K < 0 || ldw < K || ldq < (bits == 4 ? (K + 1) / 2 : K))
+    return fail(IC_ERR_ARG, "ic_quantize_weight: bad sizes");
+  if (N > 0x7fffffffLL || K > 0x7fffffffLL) return fail(IC_ERR_UNSUPPORTED, "ic_quantize_weight: dims >= 2^31");
+  if (N == 0) return IC_OK;
+  if (!w || !q || !scale) return fail(IC_ERR_ARG, "ic_quantize_weight: NULL operand");
+  return cuda_status(ic::launch_quantize_weight(w, (int)N, (int)K, ldw, bits, (uint8_t*)q, ldq, scale,
+                                                (cudaStream_t)stream),
+                     "ic_quantize_weight launch");
+}
+
+int ic_lokr_add(void* out, int dtype, int64_t M, int64_t N, const void* x, int64_t ldx, int64_t K,
+                const void* w1, int64_t out_l, int64_t in_m, const void* w2, int64_t out_k, int64_t in_n,
+                float scale, void* temp, int64_t temp_elems, void* stream) {
+  g_err[0] = 0;
+  if (dtype != IC_DTYPE_F16 && dtype != IC_DTYPE_BF16) return fail(IC_ERR_ARG, "ic_lokr_add: dtype must be f16 or bf16");
+  if (M < 0 || out_l <= 0 || in_m <= 0 || out_k <= 0 || in_n <= 0 || ldx < K)
+    return fail(IC_ERR_ARG, "ic_lokr_add: bad sizes");
+  if (out_l * out_k != N || in_m * in_n != K)
+    return fail(IC_ERR_ARG, "ic_lokr_add: factor shapes must satisfy out_l*out_k == N and in_m*in_n == K");
+  if (in_n > 256) return fail(IC_ERR_UNSUPPORTED, "ic_lokr_add: in_n (the w2 input width) must be <= 256");
+  if (out_l * in_m > 12288) return fail(IC_ERR_UNSUPPORTED, "ic_lokr_add: w1 larger than 12288 elements");
+  if (M > 0x7fffffffLL / out_l) return fail(IC_ERR_UNSUPPORTED, "ic_lokr_add: M * out_l >= 2^31");
+  if (M == 0) return IC_OK;
+  if (!out || !x || !w1 || !w2 || !temp) return fail(IC_ERR_ARG, "ic_lokr_add: NULL operand");
+  if ((__int128)temp_elems < (__int128)M * out_l * in_n) return fail(IC_ERR_ARG, "ic_lokr_add: temp needs M*out_l*in_n elements");
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = ic::launch_lokr_w1(x, dtype, (int)M, ldx, w1, (int)out_l, (int)in_m, (int)in_n, temp, st);
+  if (e != cudaSuccess) return cuda_status(e, "ic_lokr_add w1 launch");
+  // rows (t, l) of out viewed [M * out_l, out_k] (out is contiguous [M, N])
+  return cuda_status(ic::launch_lowrank_add(out, dtype, (int)(M * out_l), (int)out_k, out_k, temp, w2, (int)in_n,
+                                            scale, st),
+                     "ic_lokr_add w2 launch");
+}
+
 int ic_repack_int4(const uint8_t* src, int64_t N, int64_t K, int64_t lds, uint8_t* dst, int64_t ldd, int layout,
                    void* stream) {
   g_err[0] = 0;

@@ -4,4 +4,5 @@
 #include "prep.cu"
 #include "gemm_tc.cu"
 #include "skinny.cu"
+#include "weights.cu"
 #include "abi.cu"

@@ -100,7 +100,12 @@ class IntCrushInt4Layout:
 
     @classmethod
     def quantize(cls, tensor, scale=None, stochastic_rounding=0, inplace_ops=False):
-        """Per-row INT4 quantisation of an already rotated/permuted weight."""
+        """Per-row INT4 quantisation of an already rotated/permuted weight
+        (one B200 kernel for a CUDA weight with recalculated scales)."""
+        if _device_requant(tensor, scale):
+            from . import _b200_runtime as rt
+            packed, scales = rt.quantize_weight(tensor, 4)
+            return packed, cls.Params(scale=scales, orig_dtype=tensor.dtype, orig_shape=tuple(tensor.shape))
         amax = tensor.abs().amax(dim=1, keepdim=True)
         if scale is None or (isinstance(scale, str) and scale == "recalculate"):
             scales = (amax / INT4_SCALE_DIVISOR).clamp(min=1e-8).to(torch.float16)
@@ -115,6 +120,13 @@ class IntCrushInt4Layout:
         packed = u[..., 0::2] | (u[..., 1::2] << 4)
         params = cls.Params(scale=scales.reshape(-1), orig_dtype=tensor.dtype, orig_shape=tuple(tensor.shape))
         return packed, params
+
+
+def _device_requant(tensor, scale) -> bool:
+    """The weight is a 2-D CUDA tensor whose scales are recalculated: the
+    device kernel applies (same arithmetic as the torch form below)."""
+    recalc = scale is None or (isinstance(scale, str) and scale == "recalculate")
+    return recalc and isinstance(tensor, torch.Tensor) and tensor.is_cuda and tensor.dim() == 2
 
 
 class IntCrushInt8Layout:
@@ -149,6 +161,12 @@ class IntCrushInt8Layout:
 
     @classmethod
     def quantize(cls, tensor, scale=None, stochastic_rounding=0, inplace_ops=False):
+        """Per-row INT8 quantisation (one B200 kernel for a CUDA weight with
+        recalculated scales)."""
+        if _device_requant(tensor, scale):
+            from . import _b200_runtime as rt
+            q, scales = rt.quantize_weight(tensor, 8)
+            return q, cls.Params(scale=scales, orig_dtype=tensor.dtype, orig_shape=tuple(tensor.shape))
         amax = tensor.abs().amax(dim=1, keepdim=True)
         if scale is None or (isinstance(scale, str) and scale == "recalculate"):
             scales = (amax / INT8_SCALE_DIVISOR).clamp(min=1e-8).to(torch.float32)

@@ -176,6 +176,29 @@ int ic_gemm_a8_int8out(const int8_t* xq, int64_t M, int64_t K, int64_t ldq,
                        int8_t* c, int64_t ldc, float* s_c,
                        float* workspace, int64_t workspace_elems, void* stream);
 
+/* Requantise a float weight on the device, as the layout classes' quantize
+ * (quant_layout.py:100-129 INT4, :179-200 INT8) that set_weight calls
+ * (_ops.py:770-807): per row amax = max|w|; bits 4: scale fp16
+ * fp16(max(amax/7, 1e-8)), q = clamp(rint(w / scale), -8, 7) packed two per
+ * byte (low nibble = even column, odd K padded with 0), q [N, ldq >=
+ * ceil(K/2)] uint8; bits 8: scale fp32 max(amax/127, 1e-8),
+ * q = clamp(rint(w / scale), -128, 127), q [N, ldq >= K] int8.  IEEE
+ * division, ties to even; a 0/0 quotient stores 0.  w [N, ldw] fp32. */
+int ic_quantize_weight(const float* w, int64_t N, int64_t K, int64_t ldw, int bits,
+                       void* q, int64_t ldq, void* scale, void* stream);
+
+/* LoKr residual in place (_apply_lokr, _ops.py:88-138):
+ * out[t] viewed [out_l, out_k] += scale * (w1 @ X_t) @ w2^T, X_t = x[t]
+ * viewed [in_m, in_n]; w1 [out_l, in_m], w2 [out_k, in_n] (the combined
+ * factors; the reference's w2_t is w2 transposed).  temp = T(w1 @ X_t) is
+ * rounded to the activation dtype as the reference's matmul does, then
+ * out = T(out + scale * temp @ w2^T) with fp32 sums.  out contiguous
+ * [M, N = out_l*out_k]; x [M, ldx], K = in_m*in_n; in_n <= 256,
+ * out_l*in_m <= 12288; temp holds M*out_l*in_n elements of dtype. */
+int ic_lokr_add(void* out, int dtype, int64_t M, int64_t N, const void* x, int64_t ldx, int64_t K,
+                const void* w1, int64_t out_l, int64_t in_m, const void* w2, int64_t out_k, int64_t in_n,
+                float scale, void* temp, int64_t temp_elems, void* stream);
+
 /* ic_gemm_a8_splitk with no allocation and no caller workspace.  No
  * counterpart in the reference: it exists for callers that cannot allocate
  * device memory when they run the GEMM -- a C or FFI host without a device

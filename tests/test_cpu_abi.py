@@ -118,3 +118,19 @@ def test_int8out_workspace_and_output_checks():
     assert lib.ic_gemm_a8_int8out(*base, None, 128, f, f, 64 * 129, None) == L.IC_ERR_ARG
     zero = [f, 0] + base[2:]
     assert lib.ic_gemm_a8_int8out(*zero, f, 128, f, f, 0, None) == L.IC_OK
+
+
+def test_weight_requant_and_lokr_validation():
+    lib = L.lib()
+    f = ctypes.c_void_p(256)
+    assert lib.ic_quantize_weight(f, 4, 64, 64, 3, f, 32, f, None) == L.IC_ERR_ARG
+    assert lib.ic_quantize_weight(f, 4, 64, 64, 4, f, 31, f, None) == L.IC_ERR_ARG     # ldq < ceil(K/2)
+    assert lib.ic_quantize_weight(f, 4, 64, 64, 8, f, 32, f, None) == L.IC_ERR_ARG     # ldq < K
+    assert lib.ic_quantize_weight(None, 0, 64, 64, 8, None, 64, None, None) == L.IC_OK
+    # out_l * out_k must be N and in_m * in_n must be K
+    assert lib.ic_lokr_add(f, L.IC_DTYPE_F16, 4, 100, f, 64, 64, f, 4, 4, f, 24, 16, 1.0, f, 1 << 20,
+                           None) == L.IC_ERR_ARG
+    assert lib.ic_lokr_add(f, L.IC_DTYPE_F16, 4, 96, f, 512, 512, f, 4, 1, f, 24, 512, 1.0, f, 1 << 20,
+                           None) == L.IC_ERR_UNSUPPORTED   # in_n > 256
+    assert lib.ic_lokr_add(f, L.IC_DTYPE_F16, 4, 96, f, 64, 64, f, 4, 4, f, 24, 16, 1.0, f, 10,
+                           None) == L.IC_ERR_ARG            # temp too small

@@ -312,3 +312,47 @@ def test_convlinear_modules_on_cuda(dtype):
     tol = 1e-3 if dtype == torch.float16 else 4e-3
     assert float((y4.cpu().double() - ref4).abs().max() / ref4.abs().max()) <= tol
     assert float((y8.cpu().double() - ref8).abs().max() / ref8.abs().max()) <= tol
+
+
+class _LoKr:
+    name = "lokr"
+
+    def __init__(self, w1, w2_a, w2_b, alpha):
+        # (w1, w2, alpha, w1_a, w1_b, w2_a, w2_b): w2 from its low-rank factors
+        self.weights = (w1, None, alpha, None, None, w2_a, w2_b)
+
+
+def test_lokr_residual_through_the_layer():
+    """A LoKr adapter on an INT8 layer: the layer's output minus its plain
+    output is the Kronecker residual scale * (w1 (x) w2) x_raw (oracle in
+    fp64, A8 bar on the residual)."""
+    _dev()
+    lin = int8_layer()
+    x = h("int8_x").cuda()
+    base = lin(x).float()
+    g = torch.Generator().manual_seed(5)
+    w1 = (torch.randn(4, 4, generator=g) * 0.5).half()              # out_l = in_m = 4
+    w2_a = (torch.randn(32, 8, generator=g) * 0.1).half()           # out_k = 32 (128 / 4), rank 8
+    w2_b = (torch.randn(8, 128, generator=g) * 0.1).half()          # in_n = 128 (512 / 4)
+    lin._intcrush_adapter = _LoKr(w1, w2_a, w2_b, 4.0)
+    lin._intcrush_lora_strength = 0.5
+    y = lin(x).float()
+    w2 = w2_a.double() @ w2_b.double()
+    dW = torch.kron(w1.double(), w2) * (4.0 / 8 * 0.5)
+    res = h("int8_x").double() @ dW.T
+    assert O.max_rel((y - base).cpu().numpy(), res.numpy()) <= 2e-2
+
+
+def test_set_weight_requantises_on_device():
+    """set_weight with a float weight on CUDA requantises through the device
+    kernel: same int8 data and scales as the layout's torch form on CPU."""
+    _dev()
+    lin = int8_layer()
+    g = torch.Generator().manual_seed(9)
+    w = torch.randn(128, 512, generator=g) * 0.02
+    lin.set_weight(w.cuda())
+    q_ref, p_ref = ql.IntCrushInt8Layout.quantize(w, scale="recalculate")
+    assert torch.equal(lin.weight._qdata.cpu(), q_ref)
+    assert torch.equal(lin.weight._params.scale.cpu(), p_ref.scale)
+    y = lin(h("int8_x").cuda())
+    assert torch.isfinite(y).all()
