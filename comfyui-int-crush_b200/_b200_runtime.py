@@ -420,7 +420,7 @@ def int8_gemm_int8out(
     ``s_c``.)  Weights may be int8 or packed INT4 (``group_size`` /
     ``repacked`` as in :func:`gemm_a8`).
     """
-    _need_cuda("int8_gemm_int8out", "quantize_weight", "lokr_add", x_int8, w_int8, s_w, s_a, c_out, s_c_out, bias)
+    _need_cuda("int8_gemm_int8out", x_int8, w_int8, s_w, s_a, c_out, s_c_out, bias)
     if x_int8.dtype != torch.int8:
         raise AssertionError(f"x_int8 must be int8, got {x_int8.dtype}")
     M, K = x_int8.shape
@@ -681,7 +681,8 @@ __all__ = [
     "TRITON_AVAILABLE", "TRITON_INT4_UNPACK", "TRITON_INT8_GEMM", "TRITON_INT4_INT8_UNPACK",
     "TRITON_DYNQUANT", "TRITON_W4A8_GEMM", "TRITON_FUSED_QGD", "USE_FUSED_W8A8", "USE_CUDA_GRAPHS",
     "B200_AVAILABLE", "B200_LIBRARY_LOADED",
-    "dynamic_quantize_activation", "fused_int8_gemm_dequant", "int8_gemm_int8out", "quantize_weight", "lokr_add", "fused_quant_int8_gemm_dequant",
+    "dynamic_quantize_activation", "fused_int8_gemm_dequant", "int8_gemm_int8out", "quantize_weight", "lokr_add",
+    "fused_quant_int8_gemm_dequant",
     "fused_w4a8_gemm_dequant", "unpack_int4_to_int8", "unpack_int4_to_float16",
     "prep_quantize", "gemm_a8", "gemm_w4a16", "repack_int4", "lowrank_down", "lowrank_add", "device_error",
     "fused_layernorm_quantize", "fused_rmsnorm_quantize",

@@ -544,6 +544,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
               IC_TADD(2);
             }
             tc_fence_after();
+#if defined(IC_TRACE)
+            const long long _ti = clock64();
+#endif
             const uint64_t adesc = smem_desc_sw128(smem_u32(w_stage(sw)));
             const uint64_t bdesc = smem_desc_sw128(smem_u32(x_stage(sx)));
 #pragma unroll
@@ -560,6 +563,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
               mma_commit(&x_empty[sx]);
               if constexpr (C::I4) mma_commit(&w_empty[sw]);
             }
+#if defined(IC_TRACE)
+            atomicAdd(&g_ic_trace[13], (unsigned long long)(clock64() - _ti));
+#endif
           }
           if (!ok) break;
           if constexpr (PAIR) mma_commit2_both(&acc_full[b]);
@@ -781,6 +787,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
     bool ok = true;
     for (int wu = wu0; ok && wu < total_units; wu += wu_step) {
       const int tile = wu / a.splits, split = wu % a.splits;
+#if defined(IC_TRACE)
+      const long long _ts = clock64();
+      if (warp == 4 && lane == 0) atomicAdd(&g_ic_trace[14], 1ull);
+#endif
       int n_blk, m_blk;
       tile_nm(a, tile, n_blk, m_blk);
       const int n = n_blk * C::TILE_N + row0 + 32 * q + lane;
@@ -799,6 +809,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           const int b = uc % NB;
           // next group's scale is fetched while this group is consumed
           const float sw_next = (nvalid && u + 1 < units) ? __ldg(swrow + u + 1) * wmul : 0.f;
+#if defined(IC_TRACE)
+          if (u == 0 && warp == 4 && lane == 0) atomicAdd(&g_ic_trace[12], (unsigned long long)(clock64() - _ts));
+#endif
           IC_T0();
           if (!acc_wait(b, (uint32_t)(uc / NB) & 1u)) { ok = false; break; }
           if (warp == 4 && lane == 0) IC_TADD(3);
@@ -833,6 +846,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           sw = sw_next;
         }
         if (!ok) break;
+#if defined(IC_TRACE)
+        const long long _tst = clock64();
+#endif
 #pragma unroll
         for (int c = 0; c < (C::CPT + 31) / 32; ++c) {
           const int width = (32 * c + 32 <= C::CPT) ? 32 : 16;   // a last slice of 16 when CPT % 32 == 16
@@ -846,6 +862,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
           if (a.splits > 1) store_partial(a, v, split, mbase + 32 * c, n, nvalid, lane, width);
           else store_chunk(a, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane, width);
         }
+#if defined(IC_TRACE)
+        if (warp == 4 && lane == 0) atomicAdd(&g_ic_trace[11], (unsigned long long)(clock64() - _tst));
+#endif
       } else {
         const int b = uc % NB;
         const float sw = kF16Kind<MODE> ? 1.f : (nvalid ? __ldg(&a.s_w[n]) * wmul : 0.f);

@@ -317,10 +317,14 @@ __global__ void __maxnreg__(112) prep_tile_kernel(const PrepArgs a) {
           v[j] = act_to_d(h0);
           v[j + 1] = act_to_d(h1);
         }
-        if (amb) {   // rare: take the IEEE division for this slot's values
+        // rare (about 1 value in 900): the IEEE division for exactly those
+        // values (the test is redone), so that a warp pays for one division,
+        // not sixteen
+        if (amb) {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
-            if (c0 + j < K) {
+            if (quot_ambiguous<T>(DT<T>::to_f(in[j]) * (j & 1 ? ft2[(j >> 1) * NS + t].y : ft2[(j >> 1) * NS + t].x))
+                && c0 + j < K) {
               const float f = DT<T>::to_f(DT<T>::from_f(__ldg(a.smoothrot + c0 + j)));
               v[j] = act_to_d(DT<T>::from_f(__fdiv_rn(DT<T>::to_f(in[j]), f)));
             }
@@ -378,11 +382,13 @@ __global__ void __maxnreg__(112) prep_tile_kernel(const PrepArgs a) {
           o[e] = DT<T>::to_f(h0);
           o[e + 1] = DT<T>::to_f(h1);
         }
-        if (amb) {
+        if (amb) {   // rare: the IEEE division for those values only
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
             const uint32_t j = (e & 1) ? (opos[e >> 1] >> 16) : (opos[e >> 1] & 0xFFFFu);
-            if (j != 0xFFFFu) o[e] = DT<T>::to_f(DT<T>::from_f(__fdiv_rn(fv[e], DT<T>::to_f(DT<T>::from_f(__ldg(a.smooth + j))))));
+            if (quot_ambiguous<T>(fv[e] * (e & 1 ? ft2[(e >> 1) * NS + t].y : ft2[(e >> 1) * NS + t].x))
+                && j != 0xFFFFu)
+              o[e] = DT<T>::to_f(DT<T>::from_f(__fdiv_rn(fv[e], DT<T>::to_f(DT<T>::from_f(__ldg(a.smooth + j))))));
           }
         }
 #pragma unroll
