@@ -81,6 +81,9 @@ struct GemmArgs {
   int residual_dtype;
   long long ldr;
   float* rowmax;
+  // group-scaled tiles with a 16-bit output: the epilogue stages each slice
+  // in shared memory and writes it with a TMA bulk-tensor store (tm_o)
+  int tma_store;
 };
 
 // The activation epilogue of fused_int8_gemm_dequant
@@ -140,15 +143,22 @@ struct Cfg {
   static constexpr int NBUF = (GROUPED && BN <= 128) ? 4 : ((GROUPED && BN == 160) ? 3 : 2);
   static constexpr int MAGIC_BYTES = GROUPED ? 2048 : 0;
   static constexpr int BUDGET = 224 * 1024 - MAGIC_BYTES;
-  static constexpr int S_P = I4 ? 8 : 0;   // even: the two expansion warps own alternate stages
+  // group-scaled tiles: each epilogue warp stages its 16-bit output, one
+  // 32-token x 32-feature chunk (64-byte rows) at a time, for asynchronous
+  // TMA stores (BN <= 192 with whole chunks: wider tiles leave no room)
+  static constexpr int STG_WARP = (GROUPED && BN <= 192 && CPT % 32 == 0) ? 32 * 64 : 0;
+  static constexpr int STG_BYTES = EPI * STG_WARP;
+  // even: the two expansion warps own alternate stages
+  static constexpr int S_P = I4 ? (STG_WARP ? 6 : 8) : 0;
   static constexpr int S_W = I4 ? 4 : 0;
   static constexpr int XSTAGE = I4 ? X_BYTES : (X_BYTES + W_BYTES);
-  static constexpr int S_X_RAW = (BUDGET - S_P * P_BYTES - S_W * W_BYTES) / XSTAGE;
+  static constexpr int S_X_RAW = (BUDGET - S_P * P_BYTES - S_W * W_BYTES - STG_BYTES) / XSTAGE;
   static constexpr int S_X = S_X_RAW > 6 ? 6 : S_X_RAW;
   static constexpr int OFF_X = MAGIC_BYTES;                       // X ring
   static constexpr int OFF_W = OFF_X + S_X * XSTAGE;              // W ring (I4)
   static constexpr int OFF_P = OFF_W + S_W * W_BYTES;             // P ring (I4)
-  static constexpr int OFF_BAR = OFF_P + S_P * P_BYTES;
+  static constexpr int OFF_STG = OFF_P + S_P * P_BYTES;           // output staging (GROUPED)
+  static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
   static constexpr int TMEM_COLS_RAW = NBUF * BN;
   static constexpr int TMEM_COLS = TMEM_COLS_RAW <= 32 ? 32 : TMEM_COLS_RAW <= 64 ? 64
                                  : TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
@@ -226,22 +236,28 @@ __device__ __forceinline__ void acc2_magic(float& a0, float& a1, uint32_t r0, ui
 
 // Store 32 consecutive tokens [m0, m0 + 32) of output feature n:
 // out[m, n] = v[j] * s_a[m] + bias_n - rowsum[m] * zpc_n.  Lane j loads the
-// per-token factors of token m0 + j (coalesced) and shuffles them to all.
-template <typename T>
+// per-token factors of token m0 + j (coalesced) and shuffles them to all
+// (the zero-point row sums only when there are some).
+// STG: write the values into a staging slice in shared memory instead (row
+// j of 64 bytes = the 32 features of token m0 + j), every row, valid or not;
+// the TMA store that follows clips the rows and features outside [M, N).
+template <typename T, bool STG = false>
 __device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const float* v, int m0, int n,
-                                              bool nvalid, float bias_n, float zpc_n, int lane, int width) {
+                                              bool nvalid, float bias_n, float zpc_n, int lane, int width,
+                                              T* stg = nullptr) {
   const int ml = m0 + lane;
+  const bool has_rs = a.rowsum != nullptr;
   const float sa_l = (ml < a.M) ? __ldg(&a.s_a[ml]) : 0.f;
-  const float rs_l = (a.rowsum && ml < a.M) ? __ldg(&a.rowsum[ml]) : 0.f;
+  const float rs_l = (has_rs && ml < a.M) ? __ldg(&a.rowsum[ml]) : 0.f;
   const int jmax = nvalid ? min(width, a.M - m0) : 0;   // valid tokens in this chunk
-  T* p = out + (size_t)m0 * a.ldo + n;
+  T* p = STG ? stg + lane : out + (size_t)m0 * a.ldo + n;
   float sa_b = sa_l, rs_b = rs_l;
   const bool extra = epi_extra(a);
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const float sa = __shfl_sync(0xffffffffu, sa_b, j);
-    const float rs = __shfl_sync(0xffffffffu, rs_b, j);
-    float y = fmaf(-rs, zpc_n, fmaf(v[j], sa, bias_n));
+    float y = fmaf(v[j], sa, bias_n);
+    if (has_rs) y = fmaf(-__shfl_sync(0xffffffffu, rs_b, j), zpc_n, y);
     if (extra) {
       y = apply_act(a.act, y);
       if (a.residual && j < jmax) y += load_any(a.residual, a.residual_dtype, (size_t)(m0 + j) * a.ldr + n);
@@ -251,12 +267,12 @@ __device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const f
         if (lane == 0 && m0 + j < a.M) atomicMax(reinterpret_cast<int*>(a.rowmax) + m0 + j, __float_as_int(am));
       }
     }
-    if (j < jmax) {
+    if (STG || j < jmax) {
       if constexpr (sizeof(T) == 4) *p = y;
       else if constexpr (std::is_same<T, __half>::value) *p = __float2half_rn(y);
       else *p = __float2bfloat16_rn(y);
     }
-    p += a.ldo;
+    p += STG ? 32 : a.ldo;
     // keep the compiler from hoisting all 32 shuffles (register pressure):
     // the next 8 shuffles depend on this empty asm, issued after these stores
     if ((j & 7) == 7) asm volatile("" : "+f"(sa_b), "+f"(rs_b)::"memory");
@@ -373,7 +389,7 @@ __device__ unsigned long long g_ic_trace[16];
 template <int MODE, int BN, bool GROUPED, bool PAIR>
 __global__ void __launch_bounds__(Cfg<MODE, BN, GROUPED, PAIR>::THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-               const GemmArgs a) {
+               const __grid_constant__ CUtensorMap tm_o, const GemmArgs a) {
   using C = Cfg<MODE, BN, GROUPED, PAIR>;
   constexpr int SX = C::S_X, SW = C::S_W, SP = C::S_P;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -849,6 +865,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
 #if defined(IC_TRACE)
         const long long _tst = clock64();
 #endif
+        // 16-bit output: each 32-token chunk is staged, then written by one
+        // TMA store per warp
+        uint8_t* stg = smem + C::OFF_STG + e * C::STG_WARP;
+        const bool tstore = C::STG_WARP > 0 && a.tma_store != 0;
+        const int n_w = n_blk * C::TILE_N + row0 + 32 * q;   // first feature of this warp's slice
 #pragma unroll
         for (int c = 0; c < (C::CPT + 31) / 32; ++c) {
           const int width = (32 * c + 32 <= C::CPT) ? 32 : 16;   // a last slice of 16 when CPT % 32 == 16
@@ -859,8 +880,27 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
             v[2 * j] = in ? __uint_as_float((uint32_t)accp[in ? 16 * c + j : 0]) : 0.f;
             v[2 * j + 1] = in ? __uint_as_float((uint32_t)(accp[in ? 16 * c + j : 0] >> 32)) : 0.f;
           }
-          if (a.splits > 1) store_partial(a, v, split, mbase + 32 * c, n, nvalid, lane, width);
-          else store_chunk(a, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane, width);
+          if (tstore) {
+            // the previous chunk's store has finished reading the staging slice
+            if (lane == 0) bulk_wait_read0();
+            __syncwarp();
+            if (a.out_dtype == IC_DTYPE_F16)
+              store_chunk_t<__half, true>(a, nullptr, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane, width,
+                                          reinterpret_cast<__half*>(stg));
+            else
+              store_chunk_t<__nv_bfloat16, true>(a, nullptr, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane,
+                                                 width, reinterpret_cast<__nv_bfloat16*>(stg));
+            fence_proxy_async_smem();   // generic-proxy writes -> the TMA engine's reads
+            __syncwarp();
+            if (lane == 0 && n_w < a.N && mbase + 32 * c < a.M) {
+              tma_store_2d(&tm_o, stg, n_w, mbase + 32 * c);
+              bulk_commit();
+            }
+          } else if (a.splits > 1) {
+            store_partial(a, v, split, mbase + 32 * c, n, nvalid, lane, width);
+          } else {
+            store_chunk(a, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane, width);
+          }
         }
 #if defined(IC_TRACE)
         if (warp == 4 && lane == 0) atomicAdd(&g_ic_trace[11], (unsigned long long)(clock64() - _tst));
@@ -896,6 +936,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
 #if defined(IC_TRACE)
   if (threadIdx.x == 0) { IC_T0(); (void)_t0; }
 #endif
+  // the epilogue's bulk stores have completed before the CTA leaves
+  if (C::STG_WARP > 0 && a.tma_store && warp >= 4 && lane == 0) bulk_wait0();
   __syncthreads();
   if constexpr (PAIR) {
     // Neither CTA may leave while the other can still reach its shared
@@ -963,17 +1005,39 @@ int num_sms() {
   return n;
 }
 
+// INTCRUSH_TMA_STORE=0 keeps the group-scaled epilogue on plain stores (A/B
+// comparisons).
+static bool tma_store_enabled() {
+  static const int v = [] { const char* e = getenv("INTCRUSH_TMA_STORE"); return (e && e[0] == '0') ? 0 : 1; }();
+  return v == 1;
+}
+
 template <int MODE, int BN, bool GROUPED, bool PAIR = false>
-static cudaError_t launch_gemm_t(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a,
+static cudaError_t launch_gemm_t(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a_in,
                                  cudaStream_t st) {
   using C = Cfg<MODE, BN, GROUPED, PAIR>;
   auto kern = gemm_tc_kernel<MODE, BN, GROUPED, PAIR>;
   cudaError_t e = set_smem_once(kern, C::SMEM);
   if (e != cudaSuccess) return e;
+  GemmArgs a = a_in;
+  // group-scaled tiles with a 16-bit output (no split-K): the output tensor
+  // [M, N] as a TMA map whose box is one epilogue warp's chunk (32 features
+  // x 32 tokens); otherwise the map stays unused
+  CUtensorMap to{};
+  a.tma_store = 0;
+  if constexpr (GROUPED) {
+    const bool out16 = a.out_dtype == IC_DTYPE_F16 || a.out_dtype == IC_DTYPE_BF16;
+    const uint64_t ld_bytes = (uint64_t)a.ldo * 2;
+    if (C::STG_WARP > 0 && tma_store_enabled() && out16 && a.splits == 1 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 &&
+        ld_bytes % 16 == 0 &&
+        make_tmap(&to, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.out, (uint64_t)a.N, (uint64_t)a.M, ld_bytes, 32, 32,
+                  CU_TENSOR_MAP_SWIZZLE_NONE))
+      a.tma_store = 1;
+  }
   const int tiles = a.m_tiles * a.n_tiles * a.splits;   // work units
   if constexpr (!PAIR) {
     const int grid = tiles < num_sms() ? tiles : num_sms();
-    kern<<<grid, C::THREADS, C::SMEM, st>>>(tw, tx, a);
+    kern<<<grid, C::THREADS, C::SMEM, st>>>(tw, tx, to, a);
     return cudaGetLastError();
   } else {
     // one CTA pair (cluster of 2) per pair of SMs, persistent over the tiles
@@ -991,7 +1055,7 @@ static cudaError_t launch_gemm_t(const CUtensorMap& tw, const CUtensorMap& tx, c
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, tw, tx, a);
+    return cudaLaunchKernelEx(&cfg, kern, tw, tx, to, a);
   }
 }
 

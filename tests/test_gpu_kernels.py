@@ -369,6 +369,33 @@ def test_gemm_a8_grouped_every_tile_width(bn, monkeypatch):
     assert r.returncode == 0, r.stderr[-2000:]
 
 
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,N,ld_pad", [(1, 200, 0), (100, 384, 8), (300, 1000, 0), (777, 200, 3),
+                                        (2500, 4000, 0)])
+def test_gemm_a8_grouped_tma_store_matches_plain_store(out_dtype, M, N, ld_pad):
+    """Group-scaled tiles with a 16-bit output write through shared memory
+    and TMA bulk-tensor stores (clipped at the M / N edges; an output row
+    stride that is not a multiple of 16 bytes falls back to plain stores).
+    Both must give the bits of the fp32 epilogue value rounded once."""
+    dev = _dev()
+    K, G = 1024, 8
+    xq, wq = _int_inputs(M, N, K, seed=M + N, int4=True)
+    rng = np.random.default_rng(N)
+    s_w = _t(rng.uniform(1e-3, 2e-2, (N, G)).astype(np.float32), dev)
+    s_a = _t(rng.uniform(1e-3, 5e-2, M).astype(np.float32), dev)
+    bias = _t((rng.standard_normal(N) * 0.02).astype(np.float16), dev)
+    x, w = _t(xq, dev), _t(O.pack_int4(wq), dev)
+    y32 = rt.gemm_a8(x, w, s_w, s_a, bias=bias, out_dtype=torch.float32, group_size=128)
+    big = torch.full((M, N + ld_pad), 7.0, dtype=out_dtype, device=dev)
+    out = big[:, :N]
+    rt.gemm_a8(x, w, s_w, s_a, bias=bias, out_dtype=out_dtype, group_size=128, out=out)
+    assert torch.equal(out, y32.to(out_dtype))
+    if ld_pad:
+        assert torch.all(big[:, N:] == 7.0)   # nothing written past the slice
+    ref = O.gemm_a8(xq, s_a.cpu().numpy(), wq, s_w.cpu().numpy(), bias=bias.cpu().numpy(), group_size=128)
+    assert O.max_rel(out.float().cpu().numpy(), ref) <= 5e-3
+
+
 def test_gemm_a8_unpacked_int4_matches_packed():
     dev = _dev()
     M, N, K = 64, 256, 1024
@@ -635,7 +662,10 @@ def test_int8_gemm_int8out_row_global_scale(act, int4, G, M):
     args = (_t(xq, dev), w, _t(s_w, dev), _t(s_a, dev))
     y = rt.gemm_a8(*args, bias=bias, out_dtype=torch.float32, group_size=K // G, splits=1, activation=act)
     c, s_c = rt.int8_gemm_int8out(*args, bias=bias, activation=act, group_size=K // G)
-    s_ref = y.abs().amax(1).clamp(min=1e-8) / 127.0
+    # a tensor divisor: torch turns division by a Python scalar into a
+    # multiplication by its reciprocal, which is not the IEEE quotient
+    amax = y.abs().amax(1).clamp(min=1e-8)
+    s_ref = amax / torch.full_like(amax, 127.0)
     assert torch.equal(s_c, s_ref)
     c_ref = torch.round(y / s_ref[:, None]).clamp(-128, 127).to(torch.int8)
     assert torch.equal(c, c_ref)

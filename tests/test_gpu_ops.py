@@ -323,9 +323,8 @@ class _LoKr:
 
 
 def test_lokr_residual_through_the_layer():
-    """A LoKr adapter on an INT8 layer: the layer's output minus its plain
-    output is the Kronecker residual scale * (w1 (x) w2) x_raw (oracle in
-    fp64, A8 bar on the residual)."""
+    """A LoKr adapter on an INT8 layer adds the Kronecker residual
+    scale * (w1 (x) w2) x_raw (fp64 oracle) to the layer's plain output."""
     _dev()
     lin = int8_layer()
     x = h("int8_x").cuda()
@@ -340,7 +339,14 @@ def test_lokr_residual_through_the_layer():
     w2 = w2_a.double() @ w2_b.double()
     dW = torch.kron(w1.double(), w2) * (4.0 / 8 * 0.5)
     res = h("int8_x").double() @ dW.T
-    assert O.max_rel((y - base).cpu().numpy(), res.numpy()) <= 2e-2
+    # the residual is added to the layer's fp16 output and the sum rounded:
+    # compare y with base + res at one fp16 ulp of y plus 5e-3 of the
+    # residual's scale (its fp16 factors and intermediates); the difference
+    # y - base alone would be dominated by the fp16 rounding of two outputs
+    # ~100 times larger than the residual
+    err = (y.double().cpu() - (base.double().cpu() + res)).abs()
+    tol = y.double().cpu().abs() * 2.0 ** -10 + 5e-3 * res.abs().max()
+    assert torch.all(err <= tol), (err - tol).max().item()
 
 
 def test_set_weight_requantises_on_device():
