@@ -508,11 +508,16 @@ def gemm_w4a16(
     out: torch.Tensor | None = None,
     K: int | None = None,
     w_layout: int = 0,
+    splits: int | None = None,
 ) -> torch.Tensor:
     """W4A16: ``T(x @ W^T (+ bias))`` then ``+= lr_scale * lr_mid @ lr_up^T``,
     T = x's dtype.  fp16: ``W = fp16(q * fp16(s))`` (the Triton unpack's
     product); bf16: ``W = bf16(q * s)`` from the fp32 product (the PyTorch
     path's dequantisation cast to the activation dtype).
+
+    ``splits`` (M > 128 only): K parts run as separate work units with fp32
+    partials in a workspace allocated here; None picks the count that fills
+    the SMs (token tiles of 128), 1 runs unsplit.
 
     Replaces ``unpack_int4_to_float16`` + ``F.linear`` (``_ops.py:473-474``)
     and the PyTorch INT4 path (``_ops.py:483-491``).
@@ -540,13 +545,30 @@ def gemm_w4a16(
     mid = None if lr_mid is None else lr_mid.to(x.dtype).contiguous()
     up = None if lr_up is None else lr_up.to(x.dtype).contiguous()
     R = 0 if mid is None else mid.shape[1]
-    st = L.lib().ic_gemm_w4a16(
+    if splits is None:
+        splits = _w4a16_splits(M, N, K, x.device)
+    ws = torch.empty(splits * M * N if (splits > 1 and M > 128) else 0, dtype=torch.float32, device=x.device)
+    st = L.lib().ic_gemm_w4a16_splitk(
         _p(x2), _DT[x.dtype], M, K, x2.stride(0), _p(packed), N, packed.stride(0), int(w_layout),
         _p(sc), _DT[sc.dtype],
         G, gs, _p(b), _DT[b.dtype] if b is not None else 0, _p(mid), _p(up), R, float(lr_scale),
-        _p(out), out.stride(0), _stream(x2))
-    L.check(st, "ic_gemm_w4a16")
+        _p(out), out.stride(0), int(splits), _p(ws) if ws.numel() else None, ws.numel(), _stream(x2))
+    L.check(st, "ic_gemm_w4a16_splitk")
     return out
+
+
+def _w4a16_splits(M: int, N: int, K: int, device) -> int:
+    """The split count ``ic_gemm_w4a16_splitk`` plans for splits = 0 (token
+    tiles of 128, one work unit per SM, at most 8 parts dividing the 64-wide
+    K blocks); 1 for the M <= 128 weight-stream kernel."""
+    if M <= 128:
+        return 1
+    tiles = -(-M // 128) * -(-N // 128)
+    s = max(1, min(8, _num_sms(device) // max(tiles, 1)))
+    nkb = -(-K // 64)
+    while s > 1 and nkb % s:
+        s -= 1
+    return s
 
 
 def lowrank_down(x: torch.Tensor, down: torch.Tensor) -> torch.Tensor:

@@ -51,6 +51,8 @@ SIGNATURES: dict[str, list] = {
     "ic_lokr_add": [_P, _I, _L, _L, _P, _L, _L, _P, _L, _L, _P, _L, _L, _F, _P, _L, _P],
     "ic_gemm_a8_int8out": [_P, _L, _L, _L, _P, _I, _L, _L, _P, _L, _L, _P, _P, _I, _I, _P, _L, _P, _P, _L, _P],
     "ic_gemm_w4a16": [_P, _I, _L, _L, _L, _P, _L, _L, _I, _P, _I, _L, _L, _P, _I, _P, _P, _L, _F, _P, _L, _P],
+    "ic_gemm_w4a16_splitk": [_P, _I, _L, _L, _L, _P, _L, _L, _I, _P, _I, _L, _L, _P, _I, _P, _P, _L, _F, _P, _L,
+                             _I, _P, _L, _P],
     "ic_repack_int4": [_P, _L, _L, _L, _P, _L, _I, _P],
     "ic_lowrank_down": [_P, _L, _L, _L, _P, _L, _P, _P],
     "ic_lowrank_down_ex": [_P, _I, _L, _L, _L, _P, _L, _P, _P],

@@ -369,10 +369,11 @@ int ic_gemm_a8_splitk_noalloc(const int8_t* xq, int64_t M, int64_t K, int64_t ld
                       zp_corr, out, out_dtype, ldo, splits, ws, (int64_t)IC_NOALLOC_SCRATCH_FLOATS, stream);
 }
 
-int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const uint8_t* w, int64_t N,
-                  int64_t ldw, int w_layout, const void* scale, int scale_dtype, int64_t G, int64_t group_size,
-                  const void* bias, int bias_dtype, const void* lr_mid, const void* lr_up, int64_t R,
-                  float lr_scale, void* out, int64_t ldo, void* stream) {
+static int gemm_w4a16_impl(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const uint8_t* w,
+                           int64_t N, int64_t ldw, int w_layout, const void* scale, int scale_dtype, int64_t G,
+                           int64_t group_size, const void* bias, int bias_dtype, const void* lr_mid,
+                           const void* lr_up, int64_t R, float lr_scale, void* out, int64_t ldo, int splits,
+                           float* ws, int64_t ws_elems, void* stream) {
   g_err[0] = 0;
   if (x_dtype != IC_DTYPE_F16 && x_dtype != IC_DTYPE_BF16)
     return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: x must be fp16 or bf16");
@@ -402,18 +403,53 @@ int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
   }
   if (K % 64 || ldx % 8 || !aligned16(x) || ldw % 16 || !aligned16(w))
     return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: M > 128 needs K %% 64 == 0 and 16-byte aligned rows");
+  if (M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL)
+    return fail(IC_ERR_UNSUPPORTED, "ic_gemm_w4a16: dims >= 2^31");
   ic::GemmArgs a;
   memset(&a, 0, sizeof(a));
   a.G = (int)G; a.group_size = (int)group_size; a.w_scale = scale; a.w_scale_dtype = scale_dtype;
   a.bias = bias; a.bias_dtype = bias_dtype; a.out = out; a.out_dtype = x_dtype; a.ldo = ldo;
   a.w_repacked = w_layout;
+  int force_bn = 0;
+  if (splits < 0 || splits > 8) return fail(IC_ERR_ARG, "ic_gemm_w4a16_splitk: splits must be in [0, 8]");
+  if (splits == 0) {
+    ic::plan_w4a16_splits((int)M, (int)N, (int)K, &force_bn, &splits);
+    // the plan needs a workspace; without one (or too small a one) the GEMM runs unsplit
+    if (splits > 1 && (!ws || (__int128)ws_elems < (__int128)splits * M * N)) { splits = 1; force_bn = 0; }
+    if (splits == 1) force_bn = 0;
+  } else if (splits > 1) {
+    if (((K + 63) / 64) % splits) return fail(IC_ERR_ARG, "ic_gemm_w4a16_splitk: ceil(K / 64) must be a multiple of splits");
+    if (!ws || (__int128)ws_elems < (__int128)splits * M * N)
+      return fail(IC_ERR_ARG, "ic_gemm_w4a16_splitk: workspace needs splits*M*N floats");
+    force_bn = M <= 64 ? 64 : 128;   // the plan's token tile
+  }
+  a.splits = splits;
+  a.ws = ws;
   const char* why = "kernel launch";
-  cudaError_t e = ic::launch_gemm_w4a16_tc(x, x_dtype, (int)M, (int)K, ldx, w, (int)N, ldw, a, 0, st, &why);
+  cudaError_t e = ic::launch_gemm_w4a16_tc(x, x_dtype, (int)M, (int)K, ldx, w, (int)N, ldw, a, force_bn, st, &why);
   if (e != cudaSuccess) return cuda_status(e, why);
   if (lr_mid)
     return cuda_status(ic::launch_lowrank_add(out, x_dtype, (int)M, (int)N, ldo, lr_mid, lr_up, (int)R, lr_scale, st),
                        "ic_gemm_w4a16 low-rank launch");
   return IC_OK;
+}
+
+int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const uint8_t* w, int64_t N,
+                  int64_t ldw, int w_layout, const void* scale, int scale_dtype, int64_t G, int64_t group_size,
+                  const void* bias, int bias_dtype, const void* lr_mid, const void* lr_up, int64_t R,
+                  float lr_scale, void* out, int64_t ldo, void* stream) {
+  return gemm_w4a16_impl(x, x_dtype, M, K, ldx, w, N, ldw, w_layout, scale, scale_dtype, G, group_size, bias,
+                         bias_dtype, lr_mid, lr_up, R, lr_scale, out, ldo, 1, nullptr, 0, stream);
+}
+
+int ic_gemm_w4a16_splitk(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, const uint8_t* w,
+                         int64_t N, int64_t ldw, int w_layout, const void* scale, int scale_dtype, int64_t G,
+                         int64_t group_size, const void* bias, int bias_dtype, const void* lr_mid,
+                         const void* lr_up, int64_t R, float lr_scale, void* out, int64_t ldo, int splits,
+                         float* workspace, int64_t workspace_elems, void* stream) {
+  return gemm_w4a16_impl(x, x_dtype, M, K, ldx, w, N, ldw, w_layout, scale, scale_dtype, G, group_size, bias,
+                         bias_dtype, lr_mid, lr_up, R, lr_scale, out, ldo, splits, workspace, workspace_elems,
+                         stream);
 }
 
 int ic_lowrank_down_ex(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx, const void* down, int64_t R,

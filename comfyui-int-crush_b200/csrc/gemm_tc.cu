@@ -290,11 +290,12 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& a, const float* v, i
 }
 
 // Split-K partial of 32 consecutive tokens of feature n:
-// ws[split, m, n] = v[j] * s_a[m] (fp32; bias and zero point come in the reduce).
+// ws[split, m, n] = v[j] * s_a[m] (fp32; bias and zero point come in the
+// reduce; W4A16 has no activation scale: s_a == nullptr).
 __device__ __forceinline__ void store_partial(const GemmArgs& a, const float* v, int split, int m0, int n,
                                               bool nvalid, int lane, int width = 32) {
   const int ml = m0 + lane;
-  const float sa_b = (ml < a.M) ? __ldg(&a.s_a[ml]) : 0.f;
+  const float sa_b = (ml < a.M) ? (a.s_a ? __ldg(&a.s_a[ml]) : 1.f) : 0.f;
   const int jmax = nvalid ? min(width, a.M - m0) : 0;
   float* p = a.ws + ((size_t)split * a.M + m0) * a.N + n;
 #pragma unroll
@@ -920,9 +921,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
 #pragma unroll
           for (int j = 0; j < 32; ++j)
             v[j] = kF16Kind<MODE> ? __uint_as_float(r[j]) : (float)(int)r[j] * sw;
-          if constexpr (MODE == W_I4F) store_chunk_raw<__half>(a, v, mbase + 32 * c, n, nvalid, bias_n);
+          if (a.splits > 1) store_partial(a, v, split, mbase + 32 * c, n, nvalid, lane);
+          else if constexpr (MODE == W_I4F) store_chunk_raw<__half>(a, v, mbase + 32 * c, n, nvalid, bias_n);
           else if constexpr (MODE == W_I4B) store_chunk_raw<__nv_bfloat16>(a, v, mbase + 32 * c, n, nvalid, bias_n);
-          else if (a.splits > 1) store_partial(a, v, split, mbase + 32 * c, n, nvalid, lane);
           else store_chunk(a, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane);
         }
         tc_fence_before();
@@ -1228,9 +1229,30 @@ cudaError_t launch_gemm_w4a16_tc(const void* x, int x_dtype, int M, int K, long 
   a.M = M; a.N = N; a.K = K;
   a.num_kb = (K + 63) / 64;
   a.n_tiles = (N + kTileN - 1) / kTileN;
-  a.splits = 1;
-  a.kb_per_unit = a.num_kb;
-  return bf ? dispatch_bn<W_I4B, false>(bn, tw, tx, a, st) : dispatch_bn<W_I4F, false>(bn, tw, tx, a, st);
+  if (a.splits < 1) a.splits = 1;
+  a.kb_per_unit = a.num_kb / a.splits;
+  cudaError_t e = bf ? dispatch_bn<W_I4B, false>(bn, tw, tx, a, st) : dispatch_bn<W_I4F, false>(bn, tw, tx, a, st);
+  if (e != cudaSuccess || a.splits == 1) return e;
+  // fp32 partials [splits, M, N] -> out = RN(sum + bias), no activation scale
+  const long long mn = (long long)M * N;
+  splitk_reduce_kernel<<<(unsigned)((mn + 255) / 256), 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+// Split-K plan for the tcgen05 W4A16 path: token tiles of 128 (64 for
+// M <= 64) and as many K parts as fill the SMs with one work unit each (at
+// most 8, dividing the 64-wide K blocks).  Few output tiles leave most SMs
+// idle on a K loop of K / 64 blocks; split, each unit runs one part.
+void plan_w4a16_splits(int M, int N, int K, int* bn, int* splits) {
+  const int b = M <= 64 ? 64 : 128;
+  const long long tiles = (long long)((M + b - 1) / b) * ((N + kTileN - 1) / kTileN);
+  const int nkb = (K + 63) / 64;
+  int s = (int)(num_sms() / (tiles > 0 ? tiles : 1));
+  if (s > 8) s = 8;
+  if (s < 1) s = 1;
+  while (s > 1 && nkb % s) --s;
+  *bn = b;
+  *splits = s;
 }
 
 }  // namespace ic

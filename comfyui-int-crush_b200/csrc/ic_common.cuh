@@ -30,10 +30,12 @@ __device__ int g_ic_dev_error = 0;
 
 namespace ic {
 
-// Raise a kernel's dynamic shared-memory limit once per device (host side).
-// Later launches, including those recorded into a CUDA graph, make no
-// attribute calls.  Keyed by kernel address; a small lock-protected table.
-inline cudaError_t set_smem_once(const void* kern, int bytes) {
+// Raise a kernel's dynamic shared-memory limit once per device (host side),
+// and with carveout >= 0 its preferred shared-memory carveout (percent of
+// the unified L1).  Later launches, including those recorded into a CUDA
+// graph, make no attribute calls.  Keyed by kernel address; a small
+// lock-protected table.
+inline cudaError_t set_smem_once(const void* kern, int bytes, int carveout = -1) {
   struct Entry { const void* k; unsigned long long devs; };
   static Entry table[256];
   static int used = 0;
@@ -48,13 +50,17 @@ inline cudaError_t set_smem_once(const void* kern, int bytes) {
   if (e && (e->devs & bit)) return cudaSuccess;
   cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (r != cudaSuccess) return r;
+  if (carveout >= 0) {
+    r = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, carveout);
+    if (r != cudaSuccess) return r;
+  }
   if (!e && used < 256) { e = &table[used++]; e->k = kern; e->devs = 0; }
   if (e) e->devs |= bit;
   return cudaSuccess;
 }
 template <typename K>
-inline cudaError_t set_smem_once(K* kern, int bytes) {
-  return set_smem_once(reinterpret_cast<const void*>(kern), bytes);
+inline cudaError_t set_smem_once(K* kern, int bytes, int carveout = -1) {
+  return set_smem_once(reinterpret_cast<const void*>(kern), bytes, carveout);
 }
 
 __device__ __forceinline__ uint64_t globaltimer() {

@@ -203,8 +203,11 @@ __device__ __forceinline__ void quant_pair(float x0, float x1, float rs, int& q0
 // FT: 0 no factors, 1 SmoothRot factors (input columns), 2 SmoothQuant
 // factors (output positions).
 template <typename T, int LOG2R, bool SYL, int FT>
-// 112 registers: three 192-thread CTAs (3072-column rows) per SM.
-__global__ void __maxnreg__(112) prep_tile_kernel(const PrepArgs a) {
+// 96 registers: three 192-thread CTAs (3072-column rows) per SM.  Register
+// files are split between the four schedulers and a CTA's six warps land
+// 2/2/1/1 on them, so three CTAs need <= 5 warps' worth (16384 / (5 * 32))
+// per scheduler; at 112 registers only two CTAs fit.
+__global__ void __maxnreg__(96) prep_tile_kernel(const PrepArgs a) {
   static_assert(LOG2R == 0 || (LOG2R >= 4 && LOG2R <= 8), "rotation sizes 16..256 (or none)");
   constexpr bool ROT = LOG2R > 0;
   constexpr int R = 1 << LOG2R;
@@ -470,10 +473,10 @@ static cudaError_t launch_prep_tile(const PrepArgs& a, cudaStream_t st) {
   const TilePlan p = tile_plan(ns, (int)a.ldq, FT != 0);
   auto kern = prep_tile_kernel<T, LOG2R, SYL, FT>;
   cudaError_t e = cudaSuccess;
-  if (p.total > 48 * 1024) {
-    e = set_smem_once(kern, 110 * 1024);
-    if (e != cudaSuccess) return e;
-  }
+  // all of the unified L1 as shared memory: rows are streamed (no reuse
+  // through L1), and three CTAs of ~56 KB must fit
+  e = set_smem_once(kern, 110 * 1024, 100);
+  if (e != cudaSuccess) return e;
   int per_sm = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, ns, p.total);
   if (e != cudaSuccess) return e;

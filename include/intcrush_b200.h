@@ -254,6 +254,24 @@ int ic_gemm_w4a16(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
                   const void* lr_mid, const void* lr_up, int64_t R, float lr_scale,
                   void* out, int64_t ldo, void* stream);
 
+/* ic_gemm_w4a16 with split-K for the M > 128 (tcgen05) path: the 64-wide K
+ * blocks are cut into `splits` equal parts (1..8, dividing ceil(K / 64)),
+ * each run as its own work unit writing fp32 partials to workspace
+ * [splits, M, N]; a reduce kernel forms out = T(sum + bias).  splits = 0
+ * picks the count that fills the SMs with one unit each (token tiles of
+ * 128), falling back to 1 when workspace is NULL or smaller than
+ * splits * M * N floats.  Replaces the same callables as ic_gemm_w4a16
+ * (_ops.py:466-481 with kernels/triton_int4_unpack.py:62-88 + F.linear);
+ * the reference has no split form.  M <= 128 ignores splits (weight-stream
+ * kernel). */
+int ic_gemm_w4a16_splitk(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                         const uint8_t* w, int64_t N, int64_t ldw, int w_layout,
+                         const void* scale, int scale_dtype, int64_t G, int64_t group_size,
+                         const void* bias, int bias_dtype,
+                         const void* lr_mid, const void* lr_up, int64_t R, float lr_scale,
+                         void* out, int64_t ldo, int splits, float* workspace,
+                         int64_t workspace_elems, void* stream);
+
 /* Low-rank "down" projection mid = T(x @ down^T) with fp32 accumulation
  * (_ops.py:242, F.linear in the activation dtype T): x [M, K] (ldx),
  * down [R, K], mid [M, R], all in dtype (IC_DTYPE_F16 or IC_DTYPE_BF16). */

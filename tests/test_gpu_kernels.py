@@ -425,6 +425,43 @@ def test_w4a16_parity(M, G):
     assert O.max_rel(out.float().cpu().numpy(), ref) <= 1e-3
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("M,N,splits", [(129, 3072, None), (256, 3072, None), (256, 3072, 3), (300, 200, 4),
+                                        (512, 1024, 2), (4096, 384, None)])
+def test_w4a16_splitk_matches_unsplit_and_oracle(dtype, M, N, splits):
+    """The tcgen05 W4A16 path with K cut into parts (fp32 partials + reduce)
+    against the unsplit kernel and the dequant-linear oracle (1e-3 for fp16;
+    bf16 at two bf16 ulps)."""
+    dev = _dev()
+    K = 3072
+    rng = np.random.default_rng(M + N)
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    q = rng.integers(-8, 8, (N, K)).astype(np.int8)
+    packed = O.pack_int4(q)
+    scale = rng.uniform(1e-3, 2e-2, (N, 24)).astype(np.float16)
+    xt = _t(x, dev).to(dtype)
+    bias = _t((rng.standard_normal(N) * 0.02).astype(np.float16), dev).to(dtype)
+    got = rt.gemm_w4a16(xt, _t(packed, dev), _t(scale, dev), group_size=128, bias=bias, splits=splits)
+    one = rt.gemm_w4a16(xt, _t(packed, dev), _t(scale, dev), group_size=128, bias=bias, splits=1)
+    tol = 1e-3 if dtype == torch.float16 else 2 * 2.0 ** -8
+    assert O.max_rel(got.float().cpu().numpy(), one.float().cpu().numpy()) <= tol
+    if dtype == torch.float16:
+        w16 = O.dequant_int4_f16(packed, scale, K, 128)
+        ref_o = O.linear_f16(x, w16) + bias.float().cpu().numpy()
+        assert O.max_rel(got.float().cpu().numpy(), ref_o) <= 1e-3
+
+
+def test_w4a16_splitk_rejects_bad_splits():
+    dev = _dev()
+    x = torch.zeros(256, 3072, dtype=torch.float16, device=dev)
+    packed = torch.zeros(512, 1536, dtype=torch.uint8, device=dev)
+    scale = torch.ones(512, 24, dtype=torch.float16, device=dev)
+    with pytest.raises(Exception):
+        rt.gemm_w4a16(x, packed, scale, group_size=128, splits=5)   # 48 K blocks: not a multiple of 5
+    with pytest.raises(Exception):
+        rt.gemm_w4a16(x, packed, scale, group_size=128, splits=9)
+
+
 @pytest.mark.parametrize("M", [1, 16, 256])
 def test_w4a16_with_lora_parity(M):
     dev = _dev()
