@@ -234,10 +234,47 @@ __device__ __forceinline__ void acc2_magic(float& a0, float& a1, uint32_t r0, ui
       : "r"(r0), "r"(r1), "f"(-kMagicF), "f"(s));
 }
 
+// Rare epilogue forms of store_chunk_t (activation, residual add, INT8-out
+// row maxima, zero-point row sums): one non-inlined, rolled loop, so that the
+// common store below stays a short unrolled sequence.  The common path runs
+// once per tile from cold instruction-cache lines; with these forms inlined
+// 32 times per chunk and per output type it was several times longer.
+template <typename T, bool STG>
+__device__ __noinline__ void store_chunk_rare(const GemmArgs& a, T* out, const float* v, int m0, int n,
+                                              bool nvalid, float bias_n, float zpc_n, int lane, int width,
+                                              T* stg) {
+  const int ml = m0 + lane;
+  const bool has_rs = a.rowsum != nullptr;
+  const float sa_l = (ml < a.M) ? __ldg(&a.s_a[ml]) : 0.f;
+  const float rs_l = (has_rs && ml < a.M) ? __ldg(&a.rowsum[ml]) : 0.f;
+  const int jmax = nvalid ? min(width, a.M - m0) : 0;   // valid tokens in this chunk
+  T* p = STG ? stg + lane : out + (size_t)m0 * a.ldo + n;
+#pragma unroll 1
+  for (int j = 0; j < 32; ++j) {
+    const float sa = __shfl_sync(0xffffffffu, sa_l, j);
+    const float rs = __shfl_sync(0xffffffffu, rs_l, j);
+    float y = fmaf(v[j], sa, bias_n);
+    if (has_rs) y = fmaf(-rs, zpc_n, y);
+    y = apply_act(a.act, y);
+    if (a.residual && j < jmax) y += load_any(a.residual, a.residual_dtype, (size_t)(m0 + j) * a.ldr + n);
+    if (a.rowmax) {   // one atomic per token per warp: the max over the warp's 32 features first
+      float am = (j < jmax) ? fabsf(y) : 0.f;
+      asm("redux.sync.max.f32 %0, %0, 0xffffffff;" : "+f"(am));
+      if (lane == 0 && m0 + j < a.M) atomicMax(reinterpret_cast<int*>(a.rowmax) + m0 + j, __float_as_int(am));
+    }
+    if (STG || j < jmax) {
+      if constexpr (sizeof(T) == 4) *p = y;
+      else if constexpr (std::is_same<T, __half>::value) *p = __float2half_rn(y);
+      else *p = __float2bfloat16_rn(y);
+    }
+    p += STG ? 32 : a.ldo;
+  }
+}
+
 // Store 32 consecutive tokens [m0, m0 + 32) of output feature n:
-// out[m, n] = v[j] * s_a[m] + bias_n - rowsum[m] * zpc_n.  Lane j loads the
-// per-token factors of token m0 + j (coalesced) and shuffles them to all
-// (the zero-point row sums only when there are some).
+// out[m, n] = v[j] * s_a[m] + bias_n - rowsum[m] * zpc_n (then the optional
+// activation / residual / row maxima, store_chunk_rare).  Lane j loads the
+// per-token scale of token m0 + j (coalesced) and shuffles it to all.
 // STG: write the values into a staging slice in shared memory instead (row
 // j of 64 bytes = the 32 features of token m0 + j), every row, valid or not;
 // the TMA store that follows clips the rows and features outside [M, N).
@@ -245,28 +282,17 @@ template <typename T, bool STG = false>
 __device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const float* v, int m0, int n,
                                               bool nvalid, float bias_n, float zpc_n, int lane, int width,
                                               T* stg = nullptr) {
+  if (epi_extra(a) || a.rowsum) {
+    store_chunk_rare<T, STG>(a, out, v, m0, n, nvalid, bias_n, zpc_n, lane, width, stg);
+    return;
+  }
   const int ml = m0 + lane;
-  const bool has_rs = a.rowsum != nullptr;
-  const float sa_l = (ml < a.M) ? __ldg(&a.s_a[ml]) : 0.f;
-  const float rs_l = (has_rs && ml < a.M) ? __ldg(&a.rowsum[ml]) : 0.f;
+  float sa_b = (ml < a.M) ? __ldg(&a.s_a[ml]) : 0.f;
   const int jmax = nvalid ? min(width, a.M - m0) : 0;   // valid tokens in this chunk
   T* p = STG ? stg + lane : out + (size_t)m0 * a.ldo + n;
-  float sa_b = sa_l, rs_b = rs_l;
-  const bool extra = epi_extra(a);
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    const float sa = __shfl_sync(0xffffffffu, sa_b, j);
-    float y = fmaf(v[j], sa, bias_n);
-    if (has_rs) y = fmaf(-__shfl_sync(0xffffffffu, rs_b, j), zpc_n, y);
-    if (extra) {
-      y = apply_act(a.act, y);
-      if (a.residual && j < jmax) y += load_any(a.residual, a.residual_dtype, (size_t)(m0 + j) * a.ldr + n);
-      if (a.rowmax) {   // one atomic per token per warp: the max over the warp's 32 features first
-        float am = (j < jmax) ? fabsf(y) : 0.f;
-        asm("redux.sync.max.f32 %0, %0, 0xffffffff;" : "+f"(am));
-        if (lane == 0 && m0 + j < a.M) atomicMax(reinterpret_cast<int*>(a.rowmax) + m0 + j, __float_as_int(am));
-      }
-    }
+    const float y = fmaf(v[j], __shfl_sync(0xffffffffu, sa_b, j), bias_n);
     if (STG || j < jmax) {
       if constexpr (sizeof(T) == 4) *p = y;
       else if constexpr (std::is_same<T, __half>::value) *p = __float2half_rn(y);
@@ -275,7 +301,7 @@ __device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const f
     p += STG ? 32 : a.ldo;
     // keep the compiler from hoisting all 32 shuffles (register pressure):
     // the next 8 shuffles depend on this empty asm, issued after these stores
-    if ((j & 7) == 7) asm volatile("" : "+f"(sa_b), "+f"(rs_b)::"memory");
+    if ((j & 7) == 7) asm volatile("" : "+f"(sa_b)::"memory");
   }
 }
 
