@@ -40,7 +40,7 @@ M, K, N, GS, ROT = 4096, 3072, 12288, 128, 256
 OPS = 2.0 * M * N * K
 # DRAM read + write bytes of one config-2 GEMM launch, from an ncu capture of
 # the GEMM kernel (bench.py --kernel-probe gemm)
-GEMM_TRAFFIC = 84.1e6
+GEMM_TRAFFIC = 128.2e6
 
 
 def _pkg():
