@@ -747,13 +747,22 @@ def feature_sharded_secondary(world: int, rank: int, dev, steps: int = 5) -> dic
         plain = lin(d["x"])
         ov = lin.forward_overlapped(d["x"], chunks=4)
         same = bool(torch.equal(plain, ov))
+        # the single-GPU layer on the same inputs (every rank checks all columns)
+        rt = _pkg()
+        xq, s_a, _, _ = rt.prep_quantize(d["x"], smoothrot=d["smoothrot"], rot_size=ROT, w_in=K,
+                                         perm=d["perm"].to(torch.int32))
+        one = rt.gemm_a8(xq, rt.repack_int4(d["packed"], K, 0), d["scale"].float(), s_a, bias=d["bias"],
+                         out_dtype=torch.float16, group_size=GS, repacked=True)
+        eq = torch.tensor([float(torch.equal(plain, one))], device=dev)
+        dist.all_reduce(eq, op=dist.ReduceOp.MIN)
+        del one, xq
         t_plain = timed(lambda: lin(d["x"]))
         t_ov = timed(lambda: lin.forward_overlapped(d["x"], chunks=4))
         t_local = timed(lambda: lin.local_forward(d["x"], torch.float16))
     return {"tops": OPS / (min(t_plain, t_ov) * 1e-3) / 1e12, "ms_all_gather_after_gemm": t_plain,
             "ms_chunked_overlap": t_ov, "ms_local_gemm_only": t_local, "n_gpus": world,
             "all_gather_bytes_per_rank": M * (-(-N // world)) * 2 * (world - 1),
-            "overlapped_equals_plain": same,
+            "overlapped_equals_plain": same, "equals_single_gpu_layer": bool(eq.item() == 1.0),
             "layout": f"output-feature-sharded x{world}: N/{world} weight rows per GPU, NCCL all-gather of [M, N]"}
 
 
@@ -796,9 +805,25 @@ def flux_block_secondary(args, rank: int, world: int, local_rank: int, dev, rt, 
            "layout": f"token-sharded x{world} (one sample per GPU, no collective)",
            "linear_tops": world * blk.linear_ops(4096, 512) / (ms * 1e-3) / 1e12}
     if world > 1:
+        # one sample, the same on every rank (seed 100), split by image tokens
+        gc = torch.Generator().manual_seed(100)
+        img_c = torch.randn(1, 4096, 3072, generator=gc).half().to(dev)
+        txt_c = torch.randn(1, 512, 3072, generator=gc).half().to(dev)
+        vec_c = torch.randn(1, 3072, generator=gc).half().to(dev)
         blk.sp_group = dist.group.WORLD
         per = 4096 // world
-        mine = img[:, rank * per:(rank + 1) * per].contiguous()
+        mine = img_c[:, rank * per:(rank + 1) * per].contiguous()
+        # check: the ranks' image rows together equal the single-GPU block's
+        with torch.no_grad():
+            out_sp, _ = blk(mine, txt_c, vec_c)
+            parts = [torch.empty_like(out_sp) for _ in range(world)]
+            dist.all_gather(parts, out_sp.contiguous())
+            blk.sp_group = None
+            out_one, _ = blk(img_c, txt_c, vec_c)
+            blk.sp_group = dist.group.WORLD
+        sp_err = float((torch.cat(parts, 1).float() - out_one.float()).abs().max()
+                       / out_one.float().abs().max())
+        txt, vec = txt_c, vec_c
         ms_sp = timed_block(mine)
         kv = torch.randn(2, 1, 24, per, 128, generator=g).half().to(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -816,6 +841,7 @@ def flux_block_secondary(args, rank: int, world: int, local_rank: int, dev, rt, 
         res["sequence_parallel"] = {
             "tokens_per_s": n_tok / (ms_sp * 1e-3), "block_ms": ms_sp,
             "kv_all_gather_ms": ag.item(),
+            "max_rel_vs_single_gpu_block": sp_err,
             "layout": f"one sample over {world} GPUs: image tokens split, text replicated, K/V all-gather (NCCL)"}
         blk.sp_group = None
     return res

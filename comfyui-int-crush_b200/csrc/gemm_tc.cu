@@ -152,13 +152,15 @@ struct Cfg {
   static constexpr int S_P = I4 ? (STG_WARP ? 6 : 8) : 0;
   static constexpr int S_W = I4 ? 4 : 0;
   static constexpr int XSTAGE = I4 ? X_BYTES : (X_BYTES + W_BYTES);
-  static constexpr int S_X_RAW = (BUDGET - S_P * P_BYTES - S_W * W_BYTES - STG_BYTES) / XSTAGE;
+  static constexpr int S_X_RAW = (BUDGET - S_P * P_BYTES - S_W * W_BYTES - STG_BYTES - (STG_WARP ? EPI * CPT * 4 : 0)) / XSTAGE;
   static constexpr int S_X = S_X_RAW > 6 ? 6 : S_X_RAW;
   static constexpr int OFF_X = MAGIC_BYTES;                       // X ring
   static constexpr int OFF_W = OFF_X + S_X * XSTAGE;              // W ring (I4)
   static constexpr int OFF_P = OFF_W + S_W * W_BYTES;             // P ring (I4)
   static constexpr int OFF_STG = OFF_P + S_P * P_BYTES;           // output staging (GROUPED)
-  static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
+  static constexpr int OFF_SA = OFF_STG + STG_BYTES;              // per-token scales of the tile (staged stores)
+  static constexpr int SA_BYTES = STG_WARP ? EPI * CPT * 4 : 0;
+  static constexpr int OFF_BAR = OFF_SA + SA_BYTES;
   static constexpr int TMEM_COLS_RAW = NBUF * BN;
   static constexpr int TMEM_COLS = TMEM_COLS_RAW <= 32 ? 32 : TMEM_COLS_RAW <= 64 ? 64
                                  : TMEM_COLS_RAW <= 128 ? 128 : TMEM_COLS_RAW <= 256 ? 256 : 512;
@@ -278,21 +280,32 @@ __device__ __noinline__ void store_chunk_rare(const GemmArgs& a, T* out, const f
 // STG: write the values into a staging slice in shared memory instead (row
 // j of 64 bytes = the 32 features of token m0 + j), every row, valid or not;
 // the TMA store that follows clips the rows and features outside [M, N).
-template <typename T, bool STG = false>
+// SAS: the chunk's 32 per-token scales are already in shared memory at sa_s
+// (16-byte aligned; the same address in every lane, so broadcast loads)
+// instead of being loaded and shuffled here.
+template <typename T, bool STG = false, bool SAS = false>
 __device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const float* v, int m0, int n,
                                               bool nvalid, float bias_n, float zpc_n, int lane, int width,
-                                              T* stg = nullptr) {
+                                              T* stg = nullptr, const float* sa_s = nullptr) {
   if (epi_extra(a) || a.rowsum) {
     store_chunk_rare<T, STG>(a, out, v, m0, n, nvalid, bias_n, zpc_n, lane, width, stg);
     return;
   }
   const int ml = m0 + lane;
-  float sa_b = (ml < a.M) ? __ldg(&a.s_a[ml]) : 0.f;
+  float sa_b = (!SAS && ml < a.M) ? __ldg(&a.s_a[ml]) : 0.f;
   const int jmax = nvalid ? min(width, a.M - m0) : 0;   // valid tokens in this chunk
   T* p = STG ? stg + lane : out + (size_t)m0 * a.ldo + n;
+  float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    const float y = fmaf(v[j], __shfl_sync(0xffffffffu, sa_b, j), bias_n);
+    float sa;
+    if constexpr (SAS) {
+      if ((j & 3) == 0) s4 = *reinterpret_cast<const float4*>(sa_s + j);
+      sa = (j & 3) == 0 ? s4.x : (j & 3) == 1 ? s4.y : (j & 3) == 2 ? s4.z : s4.w;
+    } else {
+      sa = __shfl_sync(0xffffffffu, sa_b, j);
+    }
+    const float y = fmaf(v[j], sa, bias_n);
     if (STG || j < jmax) {
       if constexpr (sizeof(T) == 4) *p = y;
       else if constexpr (std::is_same<T, __half>::value) *p = __float2half_rn(y);
@@ -842,6 +855,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
       const float zpc_n = (nvalid && a.zp_corr) ? a.zp_corr[n] : 0.f;
       const int mbase = m_blk * BN + col0;
       if constexpr (GROUPED) {
+        // staged stores: this warp's per-token scales of the tile go to shared
+        // memory now (coalesced, long before the store needs them)
+        float* sa_s = reinterpret_cast<float*>(smem + C::OFF_SA) + e * C::CPT;
+        if (C::STG_WARP > 0 && a.tma_store) {
+          __syncwarp();   // the previous tile's reads of sa_s are done
+#pragma unroll
+          for (int i = 0; i < C::CPT / 32; ++i) {
+            const int m = mbase + 32 * i + lane;
+            sa_s[32 * i + lane] = m < a.M ? __ldg(&a.s_a[m]) : 0.f;
+          }
+          __syncwarp();
+        }
         unsigned long long accp[C::CPT / 2];   // fp32 pairs
 #pragma unroll
         for (int j = 0; j < C::CPT / 2; ++j) accp[j] = 0ull;
@@ -912,11 +937,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
             if (lane == 0) bulk_wait_read0();
             __syncwarp();
             if (a.out_dtype == IC_DTYPE_F16)
-              store_chunk_t<__half, true>(a, nullptr, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane, width,
-                                          reinterpret_cast<__half*>(stg));
+              store_chunk_t<__half, true, true>(a, nullptr, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane,
+                                                width, reinterpret_cast<__half*>(stg), sa_s + 32 * c);
             else
-              store_chunk_t<__nv_bfloat16, true>(a, nullptr, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n, lane,
-                                                 width, reinterpret_cast<__nv_bfloat16*>(stg));
+              store_chunk_t<__nv_bfloat16, true, true>(a, nullptr, v, mbase + 32 * c, n, nvalid, bias_n, zpc_n,
+                                                       lane, width, reinterpret_cast<__nv_bfloat16*>(stg),
+                                                       sa_s + 32 * c);
             fence_proxy_async_smem();   // generic-proxy writes -> the TMA engine's reads
             __syncwarp();
             if (lane == 0 && n_w < a.N && mbase + 32 * c < a.M) {

@@ -245,9 +245,32 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps, 2) w4a16_skinny_kernel(cons
       const T* mid = reinterpret_cast<const T*>(a.lr_mid);
       const T* up = reinterpret_cast<const T*>(a.lr_up);
       float l = 0.f;
+      const T* mr = mid + (long long)m * a.R;
+      const T* ur = up + (long long)n * a.R;
+      if ((a.R & 7) == 0 && ((reinterpret_cast<uintptr_t>(mr) | reinterpret_cast<uintptr_t>(ur)) & 15) == 0) {
+        // 16-byte loads, eight of each in flight per round (one memory
+        // latency per 64 rank instead of one per 8)
+        for (int j0 = 0; j0 < a.R; j0 += 64) {
+          uint4 mv[8], uv[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (j0 + 8 * i < a.R) {
+              mv[i] = __ldg(reinterpret_cast<const uint4*>(mr + j0) + i);
+              uv[i] = __ldg(reinterpret_cast<const uint4*>(ur + j0) + i);
+            }
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (j0 + 8 * i < a.R) {
+              const T* mh = reinterpret_cast<const T*>(&mv[i]);
+              const T* uh = reinterpret_cast<const T*>(&uv[i]);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) l = fmaf(DT<T>::to_f(mh[q]), DT<T>::to_f(uh[q]), l);
+            }
+        }
+      } else {
 #pragma unroll 8
-      for (int j = 0; j < a.R; ++j)
-        l = fmaf(DT<T>::to_f(mid[(long long)m * a.R + j]), DT<T>::to_f(up[(long long)n * a.R + j]), l);
+        for (int j = 0; j < a.R; ++j) l = fmaf(DT<T>::to_f(mr[j]), DT<T>::to_f(ur[j]), l);
+      }
       ov = DT<T>::from_f(DT<T>::to_f(ov) + a.lr_scale * l);
     }
     reinterpret_cast<T*>(a.out)[(long long)m * a.ldo + n] = ov;
