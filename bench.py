@@ -626,6 +626,30 @@ def secondary_lines(dev, flush, hbm_gbs: float, int8_peak: float, bf16_peak: flo
             "graph_bf16_frac": fl / (gms * 1e-3) / 1e12 / bf16_peak,
             "kernels": 2 if M3 <= 128 else 4,
             "note": "low-rank down + W4A16 (LoRA fused for M <= 128; split-K + reduce + low-rank add above)"}
+    # host cost of one call (tiny GEMM, host-bound): the ctypes runtime call
+    # and the same call through the torch.library op registered over it
+    import importlib
+    tops = importlib.import_module(PKG + "._torch_ops")
+    tops.register()
+    xs = torch.randint(-128, 128, (1, 256), generator=g, dtype=torch.int8).to(dev)
+    ws = torch.randint(-127, 128, (256, 256), generator=g, dtype=torch.int8).to(dev)
+    sws = torch.full((256,), 1e-2, device=dev)
+    sas = torch.full((1,), 1e-2, device=dev)
+    f16 = tops.dtype_code(torch.float16)
+
+    def host_us(fn, n=500):
+        for _ in range(20):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n):
+            fn()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) / n * 1e6
+    out["host_cost_us_per_call"] = {
+        "ctypes_runtime": host_us(lambda: rt.gemm_a8(xs, ws, sws, sas, out_dtype=torch.float16, splits=1)),
+        "torch_custom_op": host_us(lambda: torch.ops.intcrush_b200.gemm_a8(xs, ws, sws, sas, None, f16, 0, False)),
+        "note": "wall clock per call of a 1x256x256 INT8 GEMM issued back to back (GPU work ~3 us)"}
     return out
 
 
