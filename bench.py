@@ -835,29 +835,34 @@ def flux_block_secondary(args, rank: int, world: int, local_rank: int, dev, rt, 
         txt_c = torch.randn(1, 512, 3072, generator=gc).half().to(dev)
         vec_c = torch.randn(1, 3072, generator=gc).half().to(dev)
         blk.sp_group = dist.group.WORLD
-        per = 4096 // world
+        per, pt = 4096 // world, 512 // world
         mine = img_c[:, rank * per:(rank + 1) * per].contiguous()
-        # check: the ranks' image rows together equal the single-GPU block's
+        mine_t = txt_c[:, rank * pt:(rank + 1) * pt].contiguous()
+        # check: the ranks' rows together equal the single-GPU block's
         with torch.no_grad():
-            out_sp, _ = blk(mine, txt_c, vec_c)
-            parts = [torch.empty_like(out_sp) for _ in range(world)]
-            dist.all_gather(parts, out_sp.contiguous())
+            o_img, o_txt = blk(mine, mine_t, vec_c)
+            gi = [torch.empty_like(o_img) for _ in range(world)]
+            gt = [torch.empty_like(o_txt) for _ in range(world)]
+            dist.all_gather(gi, o_img.contiguous())
+            dist.all_gather(gt, o_txt.contiguous())
             blk.sp_group = None
-            out_one, _ = blk(img_c, txt_c, vec_c)
+            r_img, r_txt = blk(img_c, txt_c, vec_c)
             blk.sp_group = dist.group.WORLD
-        sp_err = float((torch.cat(parts, 1).float() - out_one.float()).abs().max()
-                       / out_one.float().abs().max())
-        txt, vec = txt_c, vec_c
+        sp_err = max(float((torch.cat(a, 1).float() - b.float()).abs().max() / b.float().abs().max())
+                     for a, b in ((gi, r_img), (gt, r_txt)))
+        txt, vec = mine_t, vec_c
         ms_sp = timed_block(mine)
+        # the block's four K/V all-gathers (image and text, K and V) alone
         kv = torch.randn(2, 1, 24, per, 128, generator=g).half().to(dev)
+        kvt = torch.randn(2, 1, 24, pt, 128, generator=g).half().to(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         for _ in range(2):
             _gather_tokens(kv[0], dist.group.WORLD)
         torch.cuda.synchronize()
         e0.record(st)
         for _ in range(steps):
-            _gather_tokens(kv[0], dist.group.WORLD)
-            _gather_tokens(kv[1], dist.group.WORLD)
+            for t4 in (kvt[0], kvt[1], kv[0], kv[1]):
+                _gather_tokens(t4, dist.group.WORLD)
         e1.record(st)
         torch.cuda.synchronize()
         ag = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
@@ -866,7 +871,7 @@ def flux_block_secondary(args, rank: int, world: int, local_rank: int, dev, rt, 
             "tokens_per_s": n_tok / (ms_sp * 1e-3), "block_ms": ms_sp,
             "kv_all_gather_ms": ag.item(),
             "max_rel_vs_single_gpu_block": sp_err,
-            "layout": f"one sample over {world} GPUs: image tokens split, text replicated, K/V all-gather (NCCL)"}
+            "layout": f"one sample over {world} GPUs: image and text tokens split, K/V all-gather (NCCL)"}
         blk.sp_group = None
     return res
 
@@ -897,14 +902,22 @@ class _QLinear:
         return y.reshape(*x.shape[:-1], y.shape[-1])
 
 
-def _gather_tokens(t, group):
-    """All-gather [B, heads, L_local, d] along the token axis over the group."""
+def _gather_tokens(t, group, async_op=False):
+    """All-gather [B, heads, L_local, d] along the token axis over the group.
+    With async_op, returns a function that waits for the gather and returns
+    the gathered tensor (the gather overlaps whatever is issued meanwhile)."""
     import torch
     import torch.distributed as dist
     t = t.contiguous()
     parts = [torch.empty_like(t) for _ in range(dist.get_world_size(group))]
-    dist.all_gather(parts, t, group=group)
-    return torch.cat(parts, dim=2)
+    work = dist.all_gather(parts, t, group=group, async_op=async_op)
+    if not async_op:
+        return torch.cat(parts, dim=2)
+
+    def done():
+        work.wait()
+        return torch.cat(parts, dim=2)
+    return done
 
 
 class FluxDoubleBlock:
@@ -920,11 +933,12 @@ class FluxDoubleBlock:
     per-sample gamma = 1 + scale, beta = shift (batch 1).
 
     With ``sp_group`` (sequence parallel, one sample over the ranks of the
-    group) ``img`` is this rank's contiguous slice of the image tokens and the
-    text tokens are replicated: each rank projects its own tokens, the image
-    tokens' K and V are all-gathered over the group (NCCL), and each rank's
-    queries attend over all keys.  Everything else is token-local, so the
-    per-rank outputs are the matching rows of the single-GPU block.
+    group) ``img`` and ``txt`` are this rank's contiguous slices of the image
+    and text tokens: each rank projects its own tokens, both streams' K and V
+    are all-gathered over the group (NCCL), and each rank's queries attend
+    over all keys (text keys first, as in the single-GPU block).  Everything
+    else is token-local, so the per-rank outputs are the matching rows of the
+    single-GPU block, and no rank repeats another's linear work.
     ``linear`` replaces the quantised layer (tests use a CPU stand-in)."""
 
     def __init__(self, rt, dev, seed=0, hidden=3072, heads=24, mlp=12288, fused_norm=True, sp_group=None,
@@ -969,9 +983,15 @@ class FluxDoubleBlock:
             q, k, v = qkv.view(B, -1, 3, nh, h // nh).permute(2, 0, 3, 1, 4)
             q = F.rms_norm(q, (h // nh,), self.qn[s])
             k = F.rms_norm(k, (h // nh,), self.kn[s])
-            if s == "img" and self.sp_group is not None:
-                k, v = _gather_tokens(k, self.sp_group), _gather_tokens(v, self.sp_group)
+            if self.sp_group is not None:
+                # the text stream's gathers run behind the image stream's
+                # projection; the image stream's are waited for at once
+                k = _gather_tokens(k, self.sp_group, async_op=True)
+                v = _gather_tokens(v, self.sp_group, async_op=True)
             qs.append(q); ks.append(k); vv.append(v)
+        if self.sp_group is not None:
+            ks = [f() for f in ks]
+            vv = [f() for f in vv]
         a = F.scaled_dot_product_attention(torch.cat(qs, 2), torch.cat(ks, 2), torch.cat(vv, 2))
         a = a.transpose(1, 2).reshape(B, -1, h)
         nt = txt.shape[1]
@@ -1154,6 +1174,9 @@ def run_block(args, rank: int, world: int, local_rank: int) -> None:
         per = 4096 // world
         img = img[:, rank * per:(rank + 1) * per].contiguous()
     txt = torch.randn(1, 512, 3072, generator=g).half().to(dev)
+    if seq:   # ... and text tokens
+        pt = 512 // world
+        txt = txt[:, rank * pt:(rank + 1) * pt].contiguous()
     vec = torch.randn(1, 3072, generator=g).half().to(dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     st = torch.cuda.current_stream()
@@ -1195,7 +1218,7 @@ def run_block(args, rank: int, world: int, local_rank: int) -> None:
         "config": {"workload": "config4 Flux double block: 4096 img + 512 txt tokens, hidden 3072, 24x128 heads, "
                                "MLP 12288, all linears INT4 W4A8 g128 rot256 perm; attention fp16 SDPA",
                    "norm": "torch ops" if args.unfused_norm else "LayerNorm + adaLN modulation fused into prep",
-                   "parallelism": (f"sequence-parallel x{world}: one sample, image tokens split, text replicated, "
+                   "parallelism": (f"sequence-parallel x{world}: one sample, image and text tokens split, "
                                    "K/V all-gather (NCCL)") if seq else
                                   f"token-sharded x{world} (one sample per GPU, no collective)",
                    "l2": "flushed (256 MB write) between timed steps"},

@@ -152,18 +152,19 @@ def _sp_worker(rank, world, port, out_q):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         img, txt, vec = _block_inputs()
-        per = img.shape[1] // world
+        per, pt = img.shape[1] // world, txt.shape[1] // world
         blk = _block(dist.group.WORLD)
         with torch.no_grad():
-            o_img, o_txt = blk(img[:, rank * per:(rank + 1) * per].contiguous(), txt, vec)
+            o_img, o_txt = blk(img[:, rank * per:(rank + 1) * per].contiguous(),
+                               txt[:, rank * pt:(rank + 1) * pt].contiguous(), vec)
         out_q.put((rank, o_img.numpy(), o_txt.numpy()))
     finally:
         dist.destroy_process_group()
 
 
 def test_sequence_parallel_block_matches_single_process():
-    """One sample split by image tokens over 2 gloo ranks (K/V all-gather)
-    gives the rows of the single-process block."""
+    """One sample split by image and text tokens over 2 gloo ranks (K/V
+    all-gather of both streams) gives the rows of the single-process block."""
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -180,5 +181,5 @@ def test_sequence_parallel_block_matches_single_process():
         r_img, r_txt = _block(None)(img, txt, vec)
     got = np.concatenate([r[1] for r in res], axis=1)
     np.testing.assert_allclose(got, r_img.numpy(), rtol=1e-4, atol=1e-4)
-    for r in res:
-        np.testing.assert_allclose(r[2], r_txt.numpy(), rtol=1e-4, atol=1e-4)
+    got_t = np.concatenate([r[2] for r in res], axis=1)
+    np.testing.assert_allclose(got_t, r_txt.numpy(), rtol=1e-4, atol=1e-4)
