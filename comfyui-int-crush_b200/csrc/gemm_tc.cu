@@ -97,6 +97,10 @@ __device__ __forceinline__ float apply_act(int act, float y) {
   return y;
 }
 __device__ __forceinline__ bool epi_extra(const GemmArgs& a) { return a.act || a.residual || a.rowmax; }
+// apply_act as one out-of-line copy: the unrolled store calls it per value
+// with the value in a register, instead of inlining the transcendental code
+// 32 times per chunk.
+__device__ __noinline__ float apply_act_call(int act, float y) { return apply_act(act, y); }
 
 // Tile index -> (weight tile, token tile).  Tiles run in groups of group_m
 // token tiles; within a group the token tile varies fastest.  A wave of CTAs
@@ -274,23 +278,16 @@ __device__ __noinline__ void store_chunk_rare(const GemmArgs& a, T* out, const f
 }
 
 // Store 32 consecutive tokens [m0, m0 + 32) of output feature n:
-// out[m, n] = v[j] * s_a[m] + bias_n - rowsum[m] * zpc_n (then the optional
-// activation / residual / row maxima, store_chunk_rare).  Lane j loads the
-// per-token scale of token m0 + j (coalesced) and shuffles it to all.
+// out[m, n] = act(v[j] * s_a[m] + bias_n), the activation (ACT) out of line
+// per value.  Lane j loads the per-token scale of token m0 + j (coalesced)
+// and shuffles it to all.
 // STG: write the values into a staging slice in shared memory instead (row
 // j of 64 bytes = the 32 features of token m0 + j), every row, valid or not;
 // the TMA store that follows clips the rows and features outside [M, N).
-// SAS: the chunk's 32 per-token scales are already in shared memory at sa_s
-// (16-byte aligned; the same address in every lane, so broadcast loads)
-// instead of being loaded and shuffled here.
-template <typename T, bool STG = false, bool SAS = false>
-__device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const float* v, int m0, int n,
-                                              bool nvalid, float bias_n, float zpc_n, int lane, int width,
-                                              T* stg = nullptr, const float* sa_s = nullptr) {
-  if (epi_extra(a) || a.rowsum) {
-    store_chunk_rare<T, STG>(a, out, v, m0, n, nvalid, bias_n, zpc_n, lane, width, stg);
-    return;
-  }
+template <typename T, bool STG, bool SAS, bool ACT>
+__device__ __forceinline__ void store_chunk_loop(const GemmArgs& a, T* out, const float* v, int m0, int n,
+                                                 bool nvalid, float bias_n, int lane, int width, T* stg,
+                                                 const float* sa_s) {
   const int ml = m0 + lane;
   float sa_b = (!SAS && ml < a.M) ? __ldg(&a.s_a[ml]) : 0.f;
   const int jmax = nvalid ? min(width, a.M - m0) : 0;   // valid tokens in this chunk
@@ -305,7 +302,8 @@ __device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const f
     } else {
       sa = __shfl_sync(0xffffffffu, sa_b, j);
     }
-    const float y = fmaf(v[j], sa, bias_n);
+    float y = fmaf(v[j], sa, bias_n);
+    if constexpr (ACT) y = apply_act_call(a.act, y);
     if (STG || j < jmax) {
       if constexpr (sizeof(T) == 4) *p = y;
       else if constexpr (std::is_same<T, __half>::value) *p = __float2half_rn(y);
@@ -315,6 +313,25 @@ __device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const f
     // keep the compiler from hoisting all 32 shuffles (register pressure):
     // the next 8 shuffles depend on this empty asm, issued after these stores
     if ((j & 7) == 7) asm volatile("" : "+f"(sa_b)::"memory");
+  }
+}
+
+// The output form of store_chunk_loop for the GEMM's epilogue.  SAS: the
+// chunk's 32 per-token scales are already in shared memory at sa_s (16-byte
+// aligned; the same address in every lane, so broadcast loads) instead of
+// being loaded and shuffled.  Activation-only epilogues use
+// their own copy of the unrolled loop; residual, row maxima and zero point
+// take store_chunk_rare.
+template <typename T, bool STG = false, bool SAS = false>
+__device__ __forceinline__ void store_chunk_t(const GemmArgs& a, T* out, const float* v, int m0, int n,
+                                              bool nvalid, float bias_n, float zpc_n, int lane, int width,
+                                              T* stg = nullptr, const float* sa_s = nullptr) {
+  if (a.residual || a.rowmax || a.rowsum) {
+    store_chunk_rare<T, STG>(a, out, v, m0, n, nvalid, bias_n, zpc_n, lane, width, stg);
+  } else if (a.act) {
+    store_chunk_loop<T, STG, SAS, true>(a, out, v, m0, n, nvalid, bias_n, lane, width, stg, sa_s);
+  } else {
+    store_chunk_loop<T, STG, SAS, false>(a, out, v, m0, n, nvalid, bias_n, lane, width, stg, sa_s);
   }
 }
 
